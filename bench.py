@@ -1,0 +1,497 @@
+#!/usr/bin/env python
+"""Paged K/V gather + append throughput on the Qwen-Image-2.1 1K-edit workload (B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step is one edit turn of the 1K config: the 4608-token cached prefix (512 text + 4096 conditioning-image
+tokens; 60 layers, 24 heads x 128, bf16, page 64, 24 GiB pool) is gathered for each of the 8 denoising steps,
+then the turn's 4096 new image tokens are appended (alloc + write + insert). Sessions are partitioned over
+GPUs (one process per GPU, no collective on the data path; `scaling: weak`).
+
+* ``value``  device-resident throughput: the turn's kernel launches (8 gathers + 1 append) replayed on
+  slot tables prepared before the timed region; CUDA events, max over ranks.
+* ``e2e``    the same turns through the public pool API (host prefix index, slot tables copied to the
+  device, kernels, and a device-to-host read of the turn's result probe).
+* ``roofline`` the gather kernel's algorithmic bytes / its CUDA-event launch time vs the measured HBM copy
+  bandwidth; DRAM traffic from the committed ncu summary.
+* ``cpu_baseline`` / ``--impl reference``: the reference's own torch ops (index_select / index_copy_) with the
+  restated prefix index on the host CPU, on a bounded sample (8 of the 60 layers).
+Inputs are far larger than L2 (6.8 GB per gather), so no L2 flush is needed between iterations.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged K/V gather+append HBM GB/s (% peak); DiT step ms at 1K/2K edit"
+L, H, D, PAGE = 60, 24, 128, 64
+TEXT, IMAGE, APPEND, STEPS_PER_TURN = 512, 4096, 4096, 8
+PREFIX = TEXT + IMAGE
+POOL_GIB = 24
+ROW = H * D * 2  # bytes of one token's K (or V) in one layer
+GATHER_BYTES = 2 * L * 2 * PREFIX * ROW + (PREFIX // PAGE) * 4
+APPEND_BYTES = 2 * L * 2 * APPEND * ROW + (APPEND // PAGE) * 4
+TURN_BYTES = STEPS_PER_TURN * GATHER_BYTES + APPEND_BYTES
+CPU_SAMPLE_LAYERS = 8
+CONFIG = {
+    "workload": "qwen_image_2.1_1k_edit_paged_prefix_kv",
+    "layers": L, "heads": H, "head_dim": D, "dtype": "bf16", "page_tokens": PAGE, "pool_gib": POOL_GIB,
+    "prefix_tokens": PREFIX, "append_tokens": APPEND, "gathers_per_turn": STEPS_PER_TURN,
+    "block_tables": "seeded random page permutation (shuffled free list)",
+    "l2": "no flush: each gather moves 6.8 GB, >> 126 MB L2",
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
+    return ap.parse_args()
+
+
+# ---- clocks ------------------------------------------------------------------------------------
+class ClockSampler(threading.Thread):
+    """Samples SM clock and clock-event reasons through NVML (read-only) while the timed region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device: int):
+        super().__init__(daemon=True)
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as exc:  # no NVML: report nothing rather than guess
+            self.err = str(exc)
+
+    def run(self):
+        while self.ok and not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                getter = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                bits = getter(self.h)
+                for bit, name in self.REASONS.items():
+                    if bits & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self.is_alive():
+            self.join(timeout=2)
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return 6650.0, "fallback (6.65 TB/s pool figure)"
+
+
+def committed_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (profiles/traffic.txt), if present."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+# ---- distributed plumbing ----------------------------------------------------------------------
+def dist_setup(args):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                              device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- the workload --------------------------------------------------------------------------------
+class Session:
+    """One edit session on one GPU: text header + a new conditioning image per turn."""
+
+    def __init__(self, pool, seed: int, device):
+        from qwenedit_b200 import keys
+
+        self.pool, self.device = pool, device
+        self.rng = np.random.default_rng(seed)
+        root = keys.root_key("dit", "Qwen/Qwen-Image-2.1", "bench", seed)
+        prev = int.from_bytes(root[:8], "little") & ((1 << 63) - 1)
+        self.text = np.empty(TEXT, np.int64)
+        for i, tok in enumerate(self.rng.integers(0, 150_000, size=TEXT)):
+            prev = keys.text_id(prev, int(tok))
+            self.text[i] = prev
+        self.turn = 0
+        self.new_kv = torch.empty(L, 2, APPEND, H, D, dtype=torch.bfloat16, device=device)
+        self.new_kv.normal_()
+        self.out = torch.empty(L, 2, PREFIX, H, D, dtype=torch.bfloat16, device=device)
+        # turn 0's prefix was computed by the DiT on a miss (hooks.py:126-139): store it whole
+        first = self.vids(0)
+        slots = pool.alloc(PREFIX)
+        pool.write(slots, torch.randn(L, 2, PREFIX, H, D, dtype=torch.bfloat16, device=device))
+        pool.insert(first, slots, owned_from=0)
+
+    def image_ids(self, turn: int) -> np.ndarray:
+        from qwenedit_b200 import keys
+
+        content = b"img" + turn.to_bytes(8, "little") + np.asarray([64, 64], np.int64).tobytes()
+        return keys.block_ids(int(self.text[-1]), content, IMAGE)
+
+    def vids(self, turn: int) -> np.ndarray:
+        return np.concatenate([self.text, self.image_ids(turn)])
+
+    def api_turn(self, gather_events=None):
+        """One turn through the public pool API; returns the prefix Match (released) and the appended slots."""
+        pool = self.pool
+        m = pool.match(self.vids(self.turn))
+        if m.length != PREFIX:
+            raise RuntimeError(f"turn {self.turn}: expected a full prefix hit, got {m.length}")
+        for s in range(STEPS_PER_TURN):
+            if gather_events is not None:
+                gather_events[s][0].record()
+            pool.gather_into(m.indices, self.out)
+            if gather_events is not None:
+                gather_events[s][1].record()
+        slots = pool.alloc(APPEND)
+        if slots is None:
+            raise RuntimeError("pool exhausted")
+        pool.write(slots, self.new_kv)
+        nxt = self.vids(self.turn + 1)
+        idx_host = np.concatenate([m.indices._qe_host[:TEXT], slots._qe_host])
+        idx = torch.from_numpy(idx_host)
+        idx._qe_host = idx_host
+        pool.insert(nxt, idx, owned_from=TEXT)
+        m.release()
+        self.turn += 1
+        return m, slots
+
+
+def run_ours(args, rank, world, local):
+    from qwenedit_b200.paged import PagedKVPool
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pool = PagedKVPool("dit", L, H, D, POOL_GIB << 30, torch.bfloat16, device, page_size=PAGE)
+    pool.index.shuffle_free(1000 + rank)
+    pool.kv.normal_()
+    sess = Session(pool, seed=rank, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    # ---- value: device-resident replay of K turns -------------------------------------------------
+    # host bookkeeping (match / alloc / insert) for warm-up + timed turns is done up front; the timed region
+    # launches exactly the turns' kernels on their slot tables (already on the device)
+    plans = []
+    for _ in range(args.warmup + args.steps):
+        m = pool.match(sess.vids(sess.turn))
+        assert m.length == PREFIX
+        pool._block_table(m.indices, m.indices._qe_host)
+        slots = pool.alloc(APPEND)
+        pool._block_table(slots, slots._qe_host)
+        idx_host = np.concatenate([m.indices._qe_host[:TEXT], slots._qe_host])
+        idx = torch.from_numpy(idx_host)
+        idx._qe_host = idx_host
+        pool.insert(sess.vids(sess.turn + 1), idx, owned_from=TEXT)
+        m.release()
+        sess.turn += 1
+        plans.append((m.indices, slots))
+    torch.cuda.synchronize()
+
+    def replay(plan, ev=None):
+        prefix_slots, append_slots = plan
+        for s in range(STEPS_PER_TURN):
+            if ev is not None:
+                ev[s][0].record(stream)
+            pool.gather_into(prefix_slots, sess.out)
+            if ev is not None:
+                ev[s][1].record(stream)
+        pool.write(append_slots, sess.new_kv)
+
+    for plan in plans[: args.warmup]:
+        replay(plan)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    launch_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(STEPS_PER_TURN)]
+                     for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for k, plan in enumerate(plans[args.warmup:]):
+        replay(plan, launch_events[k])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    elapsed_ms = max_over_ranks(t0.elapsed_time(t1), world, device)
+    gather_ms = [ev[0].elapsed_time(ev[1]) for turn in launch_events for ev in turn]
+    avg_gather_ms = max_over_ranks(statistics.mean(gather_ms), world, device)
+    if pool.device_errors():
+        raise RuntimeError("a kernel reported an out-of-range slot")
+
+    # ---- e2e: the same turns through the public API, result probe read back every turn ------------
+    probe = torch.empty(2, dtype=torch.int64, pin_memory=True)
+    h2d0 = pool.h2d_bytes
+    for _ in range(args.warmup):
+        sess.api_turn()
+    torch.cuda.synchronize()
+    h2d0 = pool.h2d_bytes
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    wall0 = time.perf_counter()
+    for _ in range(args.steps):
+        sess.api_turn()
+        # result probe: the pool's device error flag and 8 bytes of the last gathered row
+        probe_dev = torch.stack([pool._err.to(torch.int64)[0], sess.out[-1, 1, -1, -1, -4:].view(torch.int64)[0]])
+        probe.copy_(probe_dev, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        if int(probe[0]) != 0:
+            raise RuntimeError("device error flag set")
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - wall0) * 1e3
+    barrier(world)
+    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1), wall_ms), world, device)
+    h2d_per_step = (pool.h2d_bytes - h2d0) / args.steps
+    d2h_per_step = probe.numel() * probe.element_size()
+
+    result = {}
+    if not args.no_extras:
+        result = extras(pool, sess, device)
+    return dict(elapsed_ms=elapsed_ms, avg_gather_ms=avg_gather_ms, clocks=clock_info, e2e_ms=e2e_ms,
+                h2d=h2d_per_step, d2h=d2h_per_step, extras=result)
+
+
+def extras(pool, sess, device):
+    """Side measurements (outside the headline): DiT step gather at 2K, NVFP4 kernels."""
+    out = {}
+    # 2K edit: 16384 cond-image + 512 text prefix tokens, per-step gather through a random block table
+    pool.clear()
+    pool.index.shuffle_free(7)
+    T2 = 16384 + 512
+    vids = np.arange(1, T2 + 1, dtype=np.int64) + (1 << 40)
+    slots = pool.alloc(T2)
+    pool.insert(vids, slots, owned_from=0)
+    m = pool.match(vids)
+    big = torch.empty(L, 2, T2, H, D, dtype=torch.bfloat16, device=device)
+    for _ in range(2):
+        pool.gather_into(m.indices, big)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(5)]
+    for a, b in ev:
+        a.record()
+        pool.gather_into(m.indices, big)
+        b.record()
+    torch.cuda.synchronize()
+    ms2k = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    bytes2k = 2 * L * 2 * T2 * ROW
+    peak, _ = measured_peak()
+    out["dit_step_gather_2k"] = {"prefix_tokens": T2, "ms": round(ms2k, 4), "GB/s": round(bytes2k / ms2k / 1e6, 1),
+                                 "frac_of_measured_hbm": round(bytes2k / ms2k / 1e6 / peak, 4)}
+    m.release()
+    del big
+    torch.cuda.empty_cache()
+    out.update(nvfp4_extras(device, peak))
+    return out
+
+
+def _time_kernel(fn, flush, iters=10):
+    times = []
+    for i in range(iters + 3):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    return statistics.mean(times)
+
+
+def nvfp4_extras(device, peak):
+    from types import SimpleNamespace
+
+    from qwenedit_b200.fp4 import norm_scale_fp4, silu_mul_fp4
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2, rewritten between launches
+    out = {}
+    K = 3072
+    for T in (4096, 32768):
+        x = torch.randn(1, T, K, dtype=torch.bfloat16, device=device)
+        norm = SimpleNamespace(weight=(1 + 0.02 * torch.randn(K, device=device)).bfloat16(), eps=1e-6)
+        scale = (0.1 * torch.randn(1, K, device=device)).bfloat16()
+        shift = (0.1 * torch.randn(1, K, device=device)).bfloat16()
+        gs = torch.tensor([50.0], device=device)
+        ms = _time_kernel(lambda: norm_scale_fp4(x, norm, scale, None, None, gs, shift=shift), flush)
+        pad = -(-T // 128) * 128
+        nbytes = T * K * 2 + K * 2 * 3 + T * K // 2 + pad * K // 16
+        out[f"norm_scale_fp4_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+                                       "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
+    K = 12288
+    for T in (4096, 16384):
+        g = torch.randn(T, K, dtype=torch.bfloat16, device=device)
+        v = torch.randn(T, K, dtype=torch.bfloat16, device=device)
+        gs = torch.tensor([50.0], device=device)
+        ms = _time_kernel(lambda: silu_mul_fp4(g, v, gs), flush)
+        pad = -(-T // 128) * 128
+        nbytes = 2 * T * K * 2 + T * K // 2 + pad * K // 16
+        out[f"silu_mul_fp4_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+                                     "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
+    return out
+
+
+# ---- CPU: the reference's torch ops on the host --------------------------------------------------
+def cpu_turns(steps: int, warmup: int, layers: int = CPU_SAMPLE_LAYERS):
+    """Turns of the same workload with the oracle pool (index_select / index_copy_ on CPU) over `layers` of
+    the 60 layers; returns (GB/s, seconds per turn, threads)."""
+    from oracle.pool_ref import RefPagedKVPool
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    tokens = PREFIX + 3 * APPEND + PAGE
+    budget = tokens * layers * 2 * ROW
+    pool = RefPagedKVPool("dit-cpu", layers, H, D, budget, torch.bfloat16, page_size=PAGE)
+    pool.kv.normal_()
+    rng = np.random.default_rng(0)
+    text = rng.integers(1, 1 << 62, size=TEXT)
+    images = [rng.integers(1, 1 << 62, size=IMAGE) for _ in range(steps + warmup + 2)]
+    first = np.concatenate([text, images[0]])
+    pool.insert(first, pool.alloc(PREFIX), owned_from=0)
+    new_kv = torch.randn(layers, 2, APPEND, H, D).bfloat16()
+    times = []
+    for t in range(warmup + steps):
+        t0 = time.perf_counter()
+        m = pool.match(np.concatenate([text, images[t]]))
+        for _ in range(STEPS_PER_TURN):
+            pool.kv.index_select(2, m.indices)  # paged.py:113 (the gather of a scattered prefix)
+        slots = pool.alloc(APPEND)
+        pool.write(slots, new_kv)
+        pool.insert(np.concatenate([text, images[t + 1]]), torch.cat([m.indices[:TEXT], slots]), owned_from=TEXT)
+        m.release()
+        if t >= warmup:
+            times.append(time.perf_counter() - t0)
+    sample_bytes = TURN_BYTES * layers / L
+    per_turn = statistics.mean(times)
+    return sample_bytes / per_turn / 1e9, per_turn, threads
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args) if args.impl == "ours" else (
+        int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0)))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        gbs, per_turn, threads = cpu_turns(args.steps, args.warmup)
+        sample = (f"{CPU_SAMPLE_LAYERS} of {L} layers per turn (same per-layer shapes); "
+                  f"{args.steps} timed turns after {args.warmup} warm-up")
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_turn * 1e3 * L / CPU_SAMPLE_LAYERS, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": CONFIG,
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    r = run_ours(args, rank, world, local)
+    peak, peak_src = measured_peak()
+    value = TURN_BYTES * world / (r["elapsed_ms"] / args.steps) / 1e6  # GB/s over all ranks
+    achieved = GATHER_BYTES / r["avg_gather_ms"] / 1e6
+    traffic = committed_traffic("paged_gather_pages")
+    e2e = TURN_BYTES * world / (r["e2e_ms"] / args.steps) / 1e6
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, per_turn, threads = cpu_turns(steps=2, warmup=1)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"2 turns (+1 warm-up) over {CPU_SAMPLE_LAYERS} of {L} layers; reference torch ops "
+                         "(index_select / index_copy_) + restated prefix index"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(r["elapsed_ms"] / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
+            "dit_step_ms_1k": round(r["avg_gather_ms"], 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": "paged_gather (block table)",
+                         "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": GATHER_BYTES},
+            "frac_of_measured_hbm": round(value / world / peak, 4),
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": int(r["h2d"]),
+                    "d2h_bytes_per_step": int(r["d2h"])},
+            "gpu_launches": args.steps * (STEPS_PER_TURN + 1),
+            "clocks": r["clocks"],
+            "extras": r["extras"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/*
+ * qeb200.h — C ABI of libqeb200.so, the B200 (sm_100a) implementation of QwenEdit's
+ * paged prefix K/V cache and fused NVFP4 activation quantisers.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes (no torch types), and returns an
+ * int status (QE_OK == 0). On failure a human-readable message is available from qe_last_error()
+ * (thread-local). Device entry points take an explicit cudaStream_t (passed as void*) and are
+ * asynchronous with respect to the host; they never synchronise the stream.
+ *
+ * Reference interfaces replaced (paths inside the QwenEdit project, shauray8/QwenEdit):
+ *   multi_turn/cache/paged.py:40-131   PagedKVPool (match / alloc / insert / gather / write / usage / clear)
+ *   multi_turn/pipeline/hooks.py:126-139  _store_computed (2*L per-layer index_copy_)
+ *   multi_turn/cache/encoder.py:114,131-138  extra index_select / index_copy_
+ *   multi_turn/fibo/fp4.py:37-116       _e2m1 / _quantize_store / _norm_scale_fp4_kernel / _silu_mul_fp4_kernel
+ *   SGLang RadixCache + TokenToKVPoolAllocator as driven by paged.py:52-55,75,79,93,95,99,102
+ */
+#ifndef QEB200_H
+#define QEB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+enum {
+  QE_OK = 0,
+  QE_ERR_INVALID = 1,   /* bad argument: null pointer, negative size, misalignment, stale handle */
+  QE_ERR_CUDA = 2,      /* a CUDA runtime call or kernel launch failed */
+  QE_ERR_NOMEM = 3,     /* host allocation failed */
+  QE_ERR_TIMEOUT = 4,   /* a bounded device-side wait gave up (kernel returned early) */
+  QE_ERR_STATE = 5      /* misuse of an object (e.g. unlocking a node that holds no lock) */
+};
+
+/* Message for the last failing call on this thread ("" when none). */
+const char *qe_last_error(void);
+/* Library version string. */
+const char *qe_version(void);
+
+/* ---- paged K/V data movement (device) --------------------------------------------------------
+ *
+ * A "plane" is one [rows, row_bytes] slab of a pool: for the DiT pool kv[L, 2, cap+1, H, D] there
+ * are 2*L planes (layer l, K/V c) of row_bytes = H*D*elem. Plane p starts at
+ *     base + (p / planes_inner) * outer_stride + (p % planes_inner) * inner_stride      (bytes)
+ * so both the contiguous pool and strided caller views (e.g. kv[:, :, m:] of a larger tensor)
+ * are expressed without copies. Rows inside a plane are row_bytes apart (row-contiguous).
+ *
+ * Token-slot form: `slots` is a device int64 array, one pool row per token (page_size 1,
+ * the reference's token-granular RadixCache indices, paged.py:80).
+ * Block-table form: `block_table` is a device int32 array of page ids; token t lives in pool row
+ * block_table[t / page_size] * page_size + t % page_size.
+ *
+ * Requirements: row_bytes, strides and base pointers multiples of 16 bytes; slots / pages in range
+ * (checked on the device: an out-of-range slot is skipped and reported through *err_flag when
+ * err_flag is non-null; pass the pool's row count in pool_rows).
+ */
+typedef struct qe_planes {
+  void *base;            /* device pointer of plane 0 */
+  int64_t outer_stride;  /* bytes between planes p and p + planes_inner */
+  int64_t inner_stride;  /* bytes between planes p and p + 1 inside one outer group */
+  int32_t planes_inner;  /* planes per outer group (2 for K/V, 1 for a plain stack) */
+  int32_t _pad;
+} qe_planes;
+
+/* gather: out plane p row t = pool plane p row slots[t]  (paged.py:106-113, index_select dim 2;
+ * encoder.py:114 extra.index_select). n_planes planes, n_tokens rows each. */
+int qe_gather_slots(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
+                    const int64_t *slots, int64_t n_tokens, int32_t *err_flag, void *stream);
+
+/* gather through a page table (page_size tokens per page; BASELINE perf mode). */
+int qe_gather_pages(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
+                    const int32_t *block_table, int32_t page_size, int64_t n_tokens, int32_t *err_flag,
+                    void *stream);
+
+/* append (scatter): pool plane p row slots[t] = src plane p row t  (paged.py:115-116 index_copy_ dim 2;
+ * encoder.py:135 extra.index_copy_). */
+int qe_append_slots(qe_planes pool, int64_t pool_rows, qe_planes src, int32_t n_planes, int64_t row_bytes,
+                    const int64_t *slots, int64_t n_tokens, int32_t *err_flag, void *stream);
+
+/* append through a page table. */
+int qe_append_pages(qe_planes pool, int64_t pool_rows, qe_planes src, int32_t n_planes, int64_t row_bytes,
+                    const int32_t *block_table, int32_t page_size, int64_t n_tokens, int32_t *err_flag,
+                    void *stream);
+
+/* append from one source pointer per plane (hooks.py:136-138: 2*L separate index_copy_ calls from
+ * the per-layer caches layer["key"][0] / layer["value"][0]) in ONE launch. src_ptrs is a DEVICE
+ * array of n_planes device pointers; each source plane is row-contiguous ([n_tokens, row_bytes]). */
+int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs, int32_t n_planes,
+                         int64_t row_bytes, const int64_t *slots, int64_t n_tokens, int32_t *err_flag,
+                         void *stream);
+
+/* ---- fused NVFP4 activation quantisers (device) ---------------------------------------------
+ *
+ * Output contract (fibo/fp4.py:29-34, :46-61, :94-98): q [M, K/2] uint8, e2m1 pairs, low nibble =
+ * even column; sf [pad128(M), K/16] uint8 e4m3 block scales in the 128x4-swizzled layout
+ *   offset(m, g) = (m/128)*(K/64*512) + (g/4)*512 + (m%32)*16 + (m%128/32)*4 + g%4
+ * Rows M..pad128(M)-1 receive zero scales. K must be a multiple of 64. gs is a device fp32 scalar
+ * (the layer's global activation scale, pipeline/fp4.py:33-35).
+ */
+
+/* RMSNorm + adaLN scale (+ optional shift) -> NVFP4   (fibo/fp4.py:64-80, wrapper :101-109).
+ *   x [M, K] bf16 row-major (M = B*S), w [K] bf16,
+ *   noisy / clean: bf16 rows of length >= K, row b at noisy + b*mod_stride (elements; 0 = one row
+ *   shared by every batch);
+ *   mask: uint8 [S] or null (null: every token uses `noisy`); clean may be null when mask is null;
+ *   shift / shift_clean: optional bf16 adaLN shift rows with the same layout and mask select
+ *   (BASELINE's x*(1+scale)+shift; the reference has no shift). */
+int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
+                      const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S,
+                      int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream);
+
+/* SiLU(gate) * value -> NVFP4   (fibo/fp4.py:83-91, wrapper :112-116). gate, value [M, K] bf16. */
+int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
+                    uint8_t *sf, void *stream);
+
+/* ---- prefix index: radix tree + slot allocator + LRU eviction (host) -------------------------
+ *
+ * Restates the behaviour of SGLang's RadixCache (page_size 1 and paged) and TokenToKVPoolAllocator
+ * (need_sort=True) as PagedKVPool drives them (paged.py:52-55, :72-103, :118-131). Keys are int64
+ * virtual ids. Slots are pool rows 1..capacity (page mode: pages 1..capacity/page_size; page 0 is
+ * padding). Node handles are opaque 64-bit values; 0 means "no node". A handle stays valid while the
+ * node holds a lock (match + qe_index_lock). Not internally synchronised: callers serialise (the
+ * Python pool holds an RLock, paged.py:57).
+ */
+typedef struct qe_index qe_index;
+
+int qe_index_create(int64_t capacity_tokens, int32_t page_size, qe_index **out);
+int qe_index_destroy(qe_index *ix);
+/* RadixCache.reset + allocator.clear (paged.py:128-131). */
+int qe_index_clear(qe_index *ix);
+/* match_prefix (paged.py:75-80): longest cached prefix of key[0..n). Writes *out_len, the slots along
+ * the path into out_slots[0..*out_len) (capacity n), and the last node (0 when *out_len == 0).
+ * Touches the LRU clock of every node on the path and may split a node, as the reference does. */
+int qe_index_match(qe_index *ix, const int64_t *key, int64_t n, int64_t *out_len, int64_t *out_slots,
+                   uint64_t *out_node);
+/* inc_lock_ref / dec_lock_ref (paged.py:79, :36). */
+int qe_index_lock(qe_index *ix, uint64_t node);
+int qe_index_unlock(qe_index *ix, uint64_t node);
+/* insert (paged.py:99): returns the already-present prefix length in *out_present. */
+int qe_index_insert(qe_index *ix, const int64_t *key, const int64_t *slots, int64_t n, int64_t *out_present);
+/* evict up to num_tokens from unlocked leaves in LRU order (paged.py:93). Evicted slots return to
+ * the allocator. *out_evicted = tokens evicted. */
+int qe_index_evict(qe_index *ix, int64_t num_tokens, int64_t *out_evicted);
+/* allocator.alloc(n) (paged.py:95): *out_ok = 1 and n slots in out_slots, or *out_ok = 0 (no change). */
+int qe_index_alloc(qe_index *ix, int64_t n, int64_t *out_slots, int32_t *out_ok);
+/* allocator.free(slots) (paged.py:102). */
+int qe_index_free(qe_index *ix, const int64_t *slots, int64_t n);
+/* Permute the free list (seeded) so later allocations come from scattered pages. No counterpart in the
+ * reference, whose allocator starts sorted: it builds a fragmented pool for tests and benchmarks. */
+int qe_index_shuffle_free(qe_index *ix, uint64_t seed);
+/* usage (paged.py:118-126): out[0] = available slots, out[1] = evictable tokens, out[2] = protected
+ * tokens, out[3] = live tree nodes (excluding the root). */
+int qe_index_usage(qe_index *ix, int64_t out[4]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QEB200_H */

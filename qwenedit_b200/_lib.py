@@ -1,0 +1,113 @@
+"""ctypes binding of libqeb200.so (the C ABI declared in include/qeb200.h).
+
+The library is the only implementation of the path: if it is missing this module raises on first use
+(there is no CPU or PyTorch fallback). Build it with ``python -m qwenedit_b200.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_uint8, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libqeb200.so")
+
+QE_OK, QE_ERR_INVALID, QE_ERR_CUDA, QE_ERR_NOMEM, QE_ERR_TIMEOUT, QE_ERR_STATE = range(6)
+
+
+class QEError(RuntimeError):
+    """A libqeb200 call failed (CUDA error, bounded wait timeout or object misuse)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class Planes(ctypes.Structure):
+    """``qe_planes``: plane p starts at base + (p // planes_inner) * outer_stride + (p % planes_inner) * inner_stride."""
+
+    _fields_ = [("base", c_void_p), ("outer_stride", c_int64), ("inner_stride", c_int64),
+                ("planes_inner", c_int32), ("_pad", c_int32)]
+
+
+_P64 = POINTER(c_int64)
+_P32 = POINTER(c_int32)
+_PU64 = POINTER(c_uint64)
+
+# name -> (argtypes); every entry point returns int status except the two string getters
+SIGNATURES: dict[str, list] = {
+    "qe_gather_slots": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    "qe_gather_pages": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_void_p],
+    "qe_append_slots": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    "qe_append_pages": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_void_p],
+    "qe_append_slots_ptrs": [Planes, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    "qe_norm_scale_fp4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                          c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
+    "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "qe_index_create": [c_int64, c_int32, POINTER(c_void_p)],
+    "qe_index_destroy": [c_void_p],
+    "qe_index_clear": [c_void_p],
+    "qe_index_match": [c_void_p, _P64, c_int64, _P64, _P64, _PU64],
+    "qe_index_lock": [c_void_p, c_uint64],
+    "qe_index_unlock": [c_void_p, c_uint64],
+    "qe_index_insert": [c_void_p, _P64, _P64, c_int64, _P64],
+    "qe_index_evict": [c_void_p, c_int64, _P64],
+    "qe_index_alloc": [c_void_p, c_int64, _P64, _P32],
+    "qe_index_free": [c_void_p, _P64, c_int64],
+    "qe_index_usage": [c_void_p, _P64],
+    "qe_index_shuffle_free": [c_void_p, c_uint64],
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loads it once). Raises ImportError when it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise ImportError(f"{LIB_PATH.name} is not built; run `python -m qwenedit_b200.build`")
+            handle = ctypes.CDLL(str(LIB_PATH))
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = argtypes
+                fn.restype = c_int
+            handle.qe_last_error.argtypes = []
+            handle.qe_last_error.restype = c_char_p
+            handle.qe_version.argtypes = []
+            handle.qe_version.restype = c_char_p
+            _lib = handle
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call entry point `name`; map a non-zero status to ValueError (bad argument) or QEError."""
+    handle = lib()
+    status = getattr(handle, name)(*args)
+    if status != QE_OK:
+        message = f"{name}: {handle.qe_last_error().decode(errors='replace')}"
+        if status == QE_ERR_INVALID:
+            raise ValueError(message)
+        raise QEError(status, message)
+
+
+def version() -> str:
+    return lib().qe_version().decode()
+
+
+def planes(base: int, outer_stride: int, inner_stride: int, planes_inner: int) -> Planes:
+    return Planes(c_void_p(base), outer_stride, inner_stride, planes_inner, 0)
+
+
+def ptr64(array) -> "ctypes._Pointer":
+    """int64 pointer into a C-contiguous numpy int64 array."""
+    return array.ctypes.data_as(_P64)
+
+
+__all__ = ["LIB_PATH", "QEError", "Planes", "SIGNATURES", "call", "lib", "planes", "ptr64", "version",
+           "c_uint8"]
