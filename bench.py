@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
+    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu"], default=None,
+                    help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
     return ap.parse_args()
 
 
@@ -437,8 +439,54 @@ def cpu_turns(steps: int, warmup: int, layers: int = CPU_SAMPLE_LAYERS):
     return sample_bytes / per_turn / 1e9, per_turn, threads
 
 
+def profile_case(kind: str) -> None:
+    """A small case of one kernel for ncu captures: inputs > L2, a few GB on the device, 6 launches."""
+    from types import SimpleNamespace
+
+    from qwenedit_b200.fp4 import norm_scale_fp4, silu_mul_fp4
+    from qwenedit_b200.paged import PagedKVPool
+
+    device = torch.device("cuda", 0)
+    layers = CPU_SAMPLE_LAYERS  # 8 of the 60 layers: 453 MB read + 453 MB written per gather
+    times = []
+    if kind in ("gather", "append"):
+        pool = PagedKVPool("dit", layers, H, D, (PREFIX + APPEND + PAGE) * layers * 2 * ROW, torch.bfloat16, device,
+                           page_size=PAGE)
+        pool.index.shuffle_free(5)
+        pool.kv.normal_()
+        n = PREFIX if kind == "gather" else APPEND
+        slots = pool.alloc(n)
+        buf = torch.randn(layers, 2, n, H, D, device=device).bfloat16()
+        fn = (lambda: pool.gather_into(slots, buf)) if kind == "gather" else (lambda: pool.write(slots, buf))
+    elif kind == "norm":
+        T, K = 32768, 3072
+        x = torch.randn(1, T, K, dtype=torch.bfloat16, device=device)
+        norm = SimpleNamespace(weight=torch.ones(K, dtype=torch.bfloat16, device=device), eps=1e-6)
+        sc = (0.1 * torch.randn(1, K, device=device)).bfloat16()
+        gs = torch.tensor([50.0], device=device)
+        fn = lambda: norm_scale_fp4(x, norm, sc, None, None, gs, shift=sc)  # noqa: E731
+    else:
+        T, K = 4096, 12288
+        g = torch.randn(T, K, dtype=torch.bfloat16, device=device)
+        v = torch.randn(T, K, dtype=torch.bfloat16, device=device)
+        gs = torch.tensor([50.0], device=device)
+        fn = lambda: silu_mul_fp4(g, v, gs)  # noqa: E731
+    for i in range(6):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    print(json.dumps({"profile_case": kind, "ms": [round(t, 4) for t in times]}), flush=True)
+
+
 def main():
     args = parse()
+    if args.profile:
+        profile_case(args.profile)
+        return
     rank, world, local = dist_setup(args) if args.impl == "ours" else (
         int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0)))
     if args.impl == "reference":

@@ -401,12 +401,15 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   const int warps = per_warp * 8 <= kSmemMax ? 8 : 4;
   const size_t smem = per_warp * size_t(warps);
   if (smem > kSmemMax) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for one row per warp");
-  static bool attr_set[2] = {false, false};
+  // the shared-memory opt-in is per device context: remember it per device
+  static bool attr_set[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   auto kernel = warps == 8 ? qe::norm_scale_fp4_kernel<8> : qe::norm_scale_fp4_kernel<4>;
-  if (!attr_set[warps == 8]) {
+  if (!attr_set[dev][warps == 8]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemMax));
     if (e != cudaSuccess) return qe::cuda_status(e, "qe_norm_scale_fp4: smem attribute");
-    attr_set[warps == 8] = true;
+    attr_set[dev][warps == 8] = true;
   }
   const int64_t blocks_needed = (padded + warps - 1) / warps;
   const int per_sm = std::max<int>(1, int(kSmemMax / std::max<size_t>(smem, 1)));

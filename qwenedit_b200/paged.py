@@ -287,6 +287,9 @@ class PagedKVPool:
         host = self._host_slots(indices)
         self._require_cuda(indices, out)
         self._check_kv_shape(out, len(host))
+        if out.dtype != self.kv.dtype or out.stride(4) != 1 or out.stride(3) != self.head_dim or \
+                out.stride(2) != self.heads * self.head_dim:
+            raise ValueError("gather_into needs a pool-dtype output with contiguous [n, H, D] rows")
         if len(host):
             self._copy("gather", self.kv, out, indices, host, n_planes=2 * self.layers)
         return out
