@@ -79,7 +79,7 @@ class ClockSampler(threading.Thread):
     def __init__(self, device: int):
         super().__init__(daemon=True)
         self.samples, self.reasons, self.max_mhz = [], set(), None
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self.ok = False
         try:
             import pynvml
@@ -97,7 +97,7 @@ class ClockSampler(threading.Thread):
             self.err = str(exc)
 
     def run(self):
-        while self.ok and not self._stop.is_set():
+        while self.ok and not self._halt.is_set():
             try:
                 self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
                 getter = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
@@ -111,7 +111,7 @@ class ClockSampler(threading.Thread):
             time.sleep(0.05)
 
     def stop(self) -> dict:
-        self._stop.set()
+        self._halt.set()
         if self.is_alive():
             self.join(timeout=2)
         if not self.ok or not self.samples:
@@ -328,7 +328,27 @@ def run_ours(args, rank, world, local):
 
 def extras(pool, sess, device):
     """Side measurements (outside the headline): DiT step gather at 2K, NVFP4 kernels."""
+    from qwenedit_b200.paged import set_copy_mode
+
     out = {}
+    peak, _ = measured_peak()
+    # both paged-copy kernels on the 1K turn's gather and append
+    m = pool.match(sess.vids(sess.turn))
+    slots = pool.alloc(APPEND)
+    variants = {}
+    for mode in ("warp", "bulk"):
+        set_copy_mode(mode)
+        g_ms = _time_kernel(lambda: pool.gather_into(m.indices, sess.out), None, iters=5)
+        a_ms = _time_kernel(lambda: pool.write(slots, sess.new_kv), None, iters=5)
+        variants[mode] = {"gather_ms": round(g_ms, 4), "gather_GB/s": round(GATHER_BYTES / g_ms / 1e6, 1),
+                          "gather_frac": round(GATHER_BYTES / g_ms / 1e6 / peak, 4),
+                          "append_ms": round(a_ms, 4), "append_GB/s": round(APPEND_BYTES / a_ms / 1e6, 1),
+                          "append_frac": round(APPEND_BYTES / a_ms / 1e6 / peak, 4)}
+    set_copy_mode("auto")
+    m.release()
+    out["paged_copy_kernels_1k"] = variants
+    if pool.device_errors():
+        raise RuntimeError("a paged copy kernel reported an error")
     # 2K edit: 16384 cond-image + 512 text prefix tokens, per-step gather through a random block table
     pool.clear()
     pool.index.shuffle_free(7)
@@ -348,7 +368,6 @@ def extras(pool, sess, device):
     torch.cuda.synchronize()
     ms2k = statistics.mean(a.elapsed_time(b) for a, b in ev)
     bytes2k = 2 * L * 2 * T2 * ROW
-    peak, _ = measured_peak()
     out["dit_step_gather_2k"] = {"prefix_tokens": T2, "ms": round(ms2k, 4), "GB/s": round(bytes2k / ms2k / 1e6, 1),
                                  "frac_of_measured_hbm": round(bytes2k / ms2k / 1e6 / peak, 4)}
     m.release()
@@ -361,7 +380,8 @@ def extras(pool, sess, device):
 def _time_kernel(fn, flush, iters=10):
     times = []
     for i in range(iters + 3):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()

@@ -90,6 +90,11 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
                          int64_t row_bytes, const int64_t *slots, int64_t n_tokens, int32_t *err_flag,
                          void *stream);
 
+/* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel,
+ * 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned rows of <= 32 KiB,
+ * else the warp kernel). No counterpart in the reference; for measurement and tuning. */
+int qe_set_paged_copy_mode(int32_t mode);
+
 /* ---- fused NVFP4 activation quantisers (device) ---------------------------------------------
  *
  * Output contract (fibo/fp4.py:29-34, :46-61, :94-98): q [M, K/2] uint8, e2m1 pairs, low nibble =

@@ -57,6 +57,7 @@ SIGNATURES: dict[str, list] = {
     "qe_index_free": [c_void_p, _P64, c_int64],
     "qe_index_usage": [c_void_p, _P64],
     "qe_index_shuffle_free": [c_void_p, c_uint64],
+    "qe_set_paged_copy_mode": [c_int32],
 }
 
 _lock = threading.Lock()

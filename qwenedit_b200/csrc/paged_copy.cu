@@ -125,6 +125,252 @@ __global__ void __launch_bounds__(kThreads) paged_copy_kernel(CopyParams p) {
   }
 }
 
+// ---- TMA bulk-copy variant --------------------------------------------------------------------
+// One elected thread per CTA drives the copy engine: cp.async.bulk global->shared (completion counted in
+// bytes on a per-stage mbarrier) then cp.async.bulk shared->global, kStages chunks of up to kChunk bytes in
+// flight. A chunk is either a byte range of one page run (block-table form: one load, one store) or up to
+// kChunk / row_bytes consecutive tokens (slot form: one op per scattered row, one op for the contiguous
+// side). Every mbarrier wait is bounded (kWaitNs); on expiry the kernel records QE_ERR_TIMEOUT in the error
+// flag, drains what it issued (bounded again) and returns.
+constexpr int kStages = 6;
+constexpr int kChunk = 32 * 1024;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// bounded wait on an mbarrier phase; false when it gave up
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitNs) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_smem),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct BulkGeom {
+  int64_t chunks_per_plane;  // chunks of one plane
+  int64_t chunks_per_run;    // block-table form: chunks of one full page run
+  int64_t rows_per_chunk;    // slot form: tokens per chunk
+};
+
+// Issue the loads (kLoad) or the stores (!kLoad) of chunk c; returns the bytes moved into shared memory.
+template <int kMode, bool kGather, bool kPtrs, bool kLoad>
+__device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGeom &g, int64_t c, uint32_t stage,
+                                               uint32_t bar) {
+  const int32_t plane = int32_t(c / g.chunks_per_plane);
+  const int64_t rem = c - int64_t(plane) * g.chunks_per_plane;
+  char *pool_plane = p.pool.plane(plane);
+  char *oth_plane = kPtrs ? static_cast<char *>(const_cast<void *>(p.other_ptrs[plane])) : p.other.plane(plane);
+  if (kMode == kPages) {
+    const int64_t run = rem / g.chunks_per_run;
+    const int64_t k = rem - run * g.chunks_per_run;
+    const int64_t t0 = run * p.page_size;
+    const int64_t rows = min(int64_t(p.page_size), p.n_tokens - t0);
+    const int64_t off = k * kChunk;
+    const int64_t run_bytes = rows * p.row_bytes;
+    if (off >= run_bytes) return 0;
+    const uint32_t bytes = uint32_t(min(int64_t(kChunk), run_bytes - off));
+    const int64_t page = __ldg(p.pages + run);
+    if (page < 0 || (page + 1) * p.page_size > p.pool_rows) {
+      if (kLoad && p.err) atomicOr(p.err, 1);
+      return 0;
+    }
+    char *pool_ptr = pool_plane + page * p.page_size * p.row_bytes + off;
+    char *oth_ptr = oth_plane + t0 * p.row_bytes + off;
+    if (kLoad) {
+      bulk_load(stage, kGather ? pool_ptr : oth_ptr, bytes, bar);
+    } else {
+      bulk_store(kGather ? oth_ptr : pool_ptr, stage, bytes);
+    }
+    return bytes;
+  } else {
+    const int64_t t0 = rem * g.rows_per_chunk;
+    const int64_t rows = min(g.rows_per_chunk, p.n_tokens - t0);
+    if (rows <= 0) return 0;
+    const uint32_t rb = uint32_t(p.row_bytes);
+    uint32_t moved = 0;
+    // the contiguous side (gather: output rows t0..; append: source rows t0..) is one op
+    const bool contiguous_side_is_load = !kGather;
+    if (kLoad == contiguous_side_is_load) {
+      char *oth_ptr = oth_plane + t0 * p.row_bytes;
+      if (kLoad) {
+        bulk_load(stage, oth_ptr, uint32_t(rows) * rb, bar);
+      } else {
+        bulk_store(oth_ptr, stage, uint32_t(rows) * rb);
+      }
+      return uint32_t(rows) * rb;
+    }
+    for (int64_t i = 0; i < rows; ++i) {
+      const int64_t slot = __ldg(p.slots + t0 + i);
+      if (slot < 0 || slot >= p.pool_rows) {
+        if (kLoad && p.err) atomicOr(p.err, 1);
+        continue;  // skipped row: its bytes are not expected
+      }
+      char *pool_ptr = pool_plane + slot * p.row_bytes;
+      if (kLoad) {
+        bulk_load(stage + uint32_t(i) * rb, pool_ptr, rb, bar);
+      } else {
+        bulk_store(pool_ptr, stage + uint32_t(i) * rb, rb);
+      }
+      moved += rb;
+    }
+    return moved;
+  }
+}
+
+// bytes the loads of chunk c will deliver (the mbarrier's transaction count), computed before issuing
+template <int kMode, bool kGather>
+__device__ __forceinline__ uint32_t bulk_chunk_bytes(const CopyParams &p, const BulkGeom &g, int64_t c) {
+  const int32_t plane = int32_t(c / g.chunks_per_plane);
+  const int64_t rem = c - int64_t(plane) * g.chunks_per_plane;
+  if (kMode == kPages) {
+    const int64_t run = rem / g.chunks_per_run;
+    const int64_t k = rem - run * g.chunks_per_run;
+    const int64_t rows = min(int64_t(p.page_size), p.n_tokens - run * p.page_size);
+    const int64_t off = k * kChunk, run_bytes = rows * p.row_bytes;
+    if (off >= run_bytes) return 0;
+    const int64_t page = __ldg(p.pages + run);
+    if (page < 0 || (page + 1) * p.page_size > p.pool_rows) return 0;
+    return uint32_t(min(int64_t(kChunk), run_bytes - off));
+  }
+  const int64_t t0 = rem * g.rows_per_chunk;
+  const int64_t rows = min(g.rows_per_chunk, p.n_tokens - t0);
+  if (rows <= 0) return 0;
+  if (!kGather) return uint32_t(rows * p.row_bytes);
+  uint32_t bytes = 0;
+  for (int64_t i = 0; i < rows; ++i) {
+    const int64_t slot = __ldg(p.slots + t0 + i);
+    if (slot >= 0 && slot < p.pool_rows) bytes += uint32_t(p.row_bytes);
+  }
+  return bytes;
+}
+
+template <int kMode, bool kGather, bool kPtrs>
+__global__ void __launch_bounds__(32) paged_bulk_kernel(CopyParams p, BulkGeom g) {
+  extern __shared__ __align__(128) uint8_t stage_mem[];
+  __shared__ __align__(8) uint64_t bars[kStages];
+  if (threadIdx.x != 0) return;  // one thread issues every copy; the copy engine does the rest
+  const int64_t total = g.chunks_per_plane * p.n_planes;
+  const int64_t first = blockIdx.x, stride = gridDim.x;
+  const int64_t mine = first < total ? (total - first + stride - 1) / stride : 0;
+  if (mine == 0) return;
+  const uint32_t base = smem_u32(stage_mem);
+  for (int s = 0; s < kStages; ++s) mbar_init(smem_u32(&bars[s]));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+  auto issue_load = [&](int64_t i) {
+    const int64_t c = first + i * stride;
+    const uint32_t s = uint32_t(i % kStages);
+    const uint32_t bar = smem_u32(&bars[s]);
+    const uint32_t bytes = bulk_chunk_bytes<kMode, kGather>(p, g, c);
+    mbar_expect(bar, bytes);
+    if (bytes) bulk_chunk<kMode, kGather, kPtrs, true>(p, g, c, base + s * kChunk, bar);
+  };
+
+  const int64_t prologue = min(mine, int64_t(kStages));
+  for (int64_t i = 0; i < prologue; ++i) issue_load(i);
+  bool ok = true;
+  int64_t i = 0;
+  for (; i < mine; ++i) {
+    const uint32_t s = uint32_t(i % kStages);
+    if (!mbar_wait(smem_u32(&bars[s]), uint32_t((i / kStages) & 1))) {
+      ok = false;
+      break;
+    }
+    bulk_chunk<kMode, kGather, kPtrs, false>(p, g, first + i * stride, base + s * kChunk, 0);
+    bulk_commit();
+    // refill the stage of chunk i-1 once its store has finished reading shared memory
+    if (i >= 1 && i - 1 + kStages < mine) {
+      bulk_wait_read_1();
+      issue_load(i - 1 + kStages);
+    }
+  }
+  if (!ok) {
+    if (p.err) atomicOr(p.err, 2);
+    // drain the loads still in flight (each wait bounded again) so no copy lands in a retired CTA
+    const int64_t issued = min(mine, (i >= 1 ? i - 1 + kStages : int64_t(kStages)));
+    for (int64_t j = i; j < issued; ++j) mbar_wait(smem_u32(&bars[j % kStages]), uint32_t((j / kStages) & 1));
+  }
+  bulk_wait_all();
+}
+
+int bulk_launch_check(const CopyParams &p, int align) {
+  if (align < 16 || p.row_bytes > kChunk || p.row_bytes % 16) return 0;
+  return 1;
+}
+
+int g_copy_mode = 0;  // 0 auto, 1 warp LDG/STG, 2 TMA bulk
+
+template <int kMode, bool kGather, bool kPtrs>
+int launch_bulk(const CopyParams &p, cudaStream_t stream) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(paged_bulk_kernel<kMode, kGather, kPtrs>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kStages * kChunk);
+    if (e != cudaSuccess) return cuda_status(e, "paged bulk copy: smem attribute");
+    attr_done[dev] = true;
+  }
+  BulkGeom g{};
+  if (kMode == kPages) {
+    g.chunks_per_run = (int64_t(p.page_size) * p.row_bytes + kChunk - 1) / kChunk;
+    const int64_t runs = (p.n_tokens + p.page_size - 1) / p.page_size;
+    g.chunks_per_plane = runs * g.chunks_per_run;
+  } else {
+    g.rows_per_chunk = kChunk / p.row_bytes;
+    g.chunks_per_plane = (p.n_tokens + g.rows_per_chunk - 1) / g.rows_per_chunk;
+  }
+  const int64_t total = g.chunks_per_plane * p.n_planes;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(total, int64_t(sm_count())));
+  paged_bulk_kernel<kMode, kGather, kPtrs><<<dim3(unsigned(blocks)), dim3(32), kStages * kChunk, stream>>>(p, g);
+  return cuda_status(cudaGetLastError(), "paged bulk copy launch");
+}
+
 template <typename V, int kMode, bool kGather, bool kPtrs>
 int launch_typed(const CopyParams &p, cudaStream_t stream) {
   static int blocks_per_sm = 0;
@@ -150,6 +396,7 @@ bool planes_aligned(const qe_planes &pl, int a) {
 
 template <int kMode, bool kGather, bool kPtrs>
 int launch(const CopyParams &p, int align, cudaStream_t stream) {
+  if (g_copy_mode == 2 && bulk_launch_check(p, align)) return launch_bulk<kMode, kGather, kPtrs>(p, stream);
   if (align >= 16) return launch_typed<int4, kMode, kGather, kPtrs>(p, stream);
   if (align >= 4) return launch_typed<uint32_t, kMode, kGather, kPtrs>(p, stream);
   return launch_typed<uint8_t, kMode, kGather, kPtrs>(p, stream);
@@ -291,6 +538,12 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
   // alignment before uploading the array, so the width follows the pool and the row size.
   s = qe::launch<qe::kSlots, false, true>(p, qe::align_of(pool, nullptr, row_bytes), static_cast<cudaStream_t>(stream));
   return s ? s : qe::ok();
+}
+
+int qe_set_paged_copy_mode(int32_t mode) {
+  if (mode < 0 || mode > 2) return fail(QE_ERR_INVALID, "qe_set_paged_copy_mode: mode must be 0, 1 or 2");
+  qe::g_copy_mode = mode;
+  return qe::ok();
 }
 
 const char *qe_version(void) { return "qeb200 0.1.0 (sm_100a)"; }

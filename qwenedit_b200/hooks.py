@@ -1,0 +1,138 @@
+"""Pool call sites of the DiT and text-encoder prefix caches, on the B200 pool.
+
+Drop-in for the pool-facing parts of
+  multi_turn/pipeline/encoding.py:34-49     MTCaches (per-request caches, vids, prefix lengths, held matches)
+  multi_turn/pipeline/hooks.py:81-83        _set_caches       (per-layer views of a gathered prefix)
+  multi_turn/pipeline/hooks.py:86-123       _fill_from_pool   (full hit / partial reuse / miss per sample)
+  multi_turn/pipeline/hooks.py:126-139      _store_computed   (after a miss: 2*L index_copy_ -> ONE launch)
+  multi_turn/cache/encoder.py:111-138       _encode's pool hit and _store (K/V planes + hidden-state rows)
+
+The model compute that sits between them (the DiT tail prefill, cache/prefill.py:32-72, and the encoder
+tail forward, cache/encoder.py:141-203) stays with the caller: ``fill_from_pool`` takes it as a callback.
+Per-layer caches are any objects with ``update(key=..., value=...)`` and ``[...]`` access to "key" / "value",
+as the SGLang DiT's joint-attention caches are.
+"""
+
+from __future__ import annotations
+
+import logging
+import time
+from typing import Callable
+
+import numpy as np
+import torch
+
+from qwenedit_b200 import state
+from qwenedit_b200.paged import Match, PagedKVPool, cat_slots
+
+logger = logging.getLogger(__name__)
+
+
+class MTCaches(list):
+    """Per-request prefix caches (encoding.py:34-49): one list of per-layer caches per sample, the samples'
+    virtual ids and prefix lengths, and the matches held until the request ends."""
+
+    def __init__(self, caches, vids, prefix_lengths):
+        super().__init__(caches)
+        self.vids = vids
+        self.prefix_lengths = prefix_lengths
+        self.prepared = False
+        self.matches: list[Match] = []
+
+    def release(self) -> None:
+        for match in self.matches:
+            match.release()
+        self.matches.clear()
+
+    def __del__(self):
+        self.release()
+
+
+def set_caches(caches, sample: int, kv: torch.Tensor) -> None:
+    """Point each layer's joint-attention cache at its [1, n, H, D] K and V views of `kv` (no copy)."""
+    for layer in range(kv.shape[0]):
+        caches[sample][layer].update(key=kv[layer, 0][None], value=kv[layer, 1][None])
+
+
+# prefill(sample, kv, start): fill kv[:, :, start:] ([L, 2, total, H, D]) for prefix positions start.. of `sample`
+Prefill = Callable[[int, torch.Tensor, int], None]
+
+
+def fill_from_pool(pool: PagedKVPool, caches: MTCaches, prefill: Prefill | None = None) -> list[int]:
+    """Serve each sample's prefix from the pool; returns the samples that missed (to store after the forward).
+
+    * full hit: the prefix is gathered once (a view when the slots are one run) and kept locked;
+    * partial hit of at least MULTI_TURN_MIN_REUSE tokens: the head is gathered into a fresh [L, 2, total, H, D]
+      buffer, `prefill` computes the tail, and the tail is appended and inserted (owned from the match);
+    * otherwise: a miss.
+    """
+    pending = []
+    for sample, vids in enumerate(caches.vids):
+        if vids is None:
+            continue
+        t0 = time.perf_counter()
+        total = caches.prefix_lengths[sample]
+        match = pool.match(vids)
+        m = match.length
+        if m == total:
+            set_caches(caches, sample, pool.gather(match.indices))
+            caches.matches.append(match)
+        elif m >= state.MIN_REUSE and prefill is not None:
+            kv = torch.empty(pool.layers, 2, total, pool.heads, pool.head_dim, device=pool.kv.device,
+                             dtype=pool.kv.dtype)
+            pool.gather_into(match.indices, kv[:, :, :m])
+            prefill(sample, kv, m)
+            set_caches(caches, sample, kv)
+            slots = pool.alloc(total - m)
+            if slots is not None:
+                pool.write(slots, kv[:, :, m:])
+                pool.insert(vids, cat_slots(match.indices, slots), owned_from=m)
+            match.release()
+        else:
+            match.release()
+            pending.append(sample)
+            m = 0
+        if state.DEBUG:
+            logger.info("qwenedit_b200: dit sample %d reused %d/%d prefix tokens in %.1f ms", sample, m, total,
+                        (time.perf_counter() - t0) * 1e3)
+    return pending
+
+
+def store_computed(pool: PagedKVPool, caches: MTCaches, pending: list[int]) -> None:
+    """After a miss, copy every layer's freshly computed prefix K/V into the pool in one launch and insert it."""
+    for sample in pending:
+        layers = caches[sample]
+        if not layers[0]:
+            continue
+        total = caches.prefix_lengths[sample]
+        slots = pool.alloc(total)
+        if slots is None:
+            continue
+        pool.write_layers(slots, [layer["key"][0] for layer in layers], [layer["value"][0] for layer in layers])
+        pool.insert(caches.vids[sample], slots, owned_from=0)
+
+
+# ---- text encoder ------------------------------------------------------------------------------
+def encoder_hit(pool: PagedKVPool, match: Match, total: int) -> torch.Tensor | None:
+    """The full-hit branch of encoder.py:113-114: the cached hidden states of all `total` tokens, else None."""
+    if match.length != total or match.indices is None:
+        return None
+    return pool.gather_extra(match.indices)
+
+
+def encoder_store(pool: PagedKVPool, vids, match: Match | None, kv_new: torch.Tensor, hidden_new: torch.Tensor,
+                  m: int) -> bool:
+    """encoder.py:131-138: store the new tokens' K/V planes [L, 2, n, H, D] and hidden rows [n, hidden].
+    Returns False (nothing stored) when the pool cannot make room."""
+    slots = pool.alloc(kv_new.shape[2])
+    if slots is None:
+        return False
+    pool.write(slots, kv_new)
+    pool.write_extra(slots, hidden_new)
+    indices = cat_slots(match.indices, slots) if m else slots
+    pool.insert(vids, indices, owned_from=m)
+    return True
+
+
+__all__ = ["MTCaches", "set_caches", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store"]
+_ = np

@@ -147,6 +147,23 @@ def _slots_tensor(host: np.ndarray, pool: "PagedKVPool") -> torch.Tensor:
     return t
 
 
+COPY_MODES = {"auto": 0, "warp": 1, "bulk": 2}
+
+
+def set_copy_mode(mode: str) -> None:
+    """Select the paged copy kernel process-wide: "auto", "warp" (vectorised LDG/STG) or "bulk" (TMA bulk copies)."""
+    _lib.call("qe_set_paged_copy_mode", COPY_MODES[mode])
+
+
+def cat_slots(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``torch.cat([a, b])`` of slot tensors, keeping the host mirror when both carry one."""
+    out = torch.cat([a, b])
+    ha, hb = getattr(a, "_qe_host", None), getattr(b, "_qe_host", None)
+    if ha is not None and hb is not None:
+        out._qe_host = np.concatenate([ha, hb])
+    return out
+
+
 class PagedKVPool:
     """Paged K/V prefix pool on one GPU (paged.py:40-131)."""
 
@@ -164,6 +181,8 @@ class PagedKVPool:
         self.extra_dim = extra_dim
         self.rows = self.capacity + self.page_size  # row 0 (page 0) is the allocator's padding
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.kv = torch.empty(layers, 2, self.rows, heads, head_dim, dtype=dtype, device=self.device)
         self.extra = (
             torch.empty(self.rows, extra_dim, dtype=dtype, device=self.device) if extra_dim else None

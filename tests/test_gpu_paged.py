@@ -14,6 +14,16 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+@pytest.fixture(autouse=True, params=["warp", "bulk"])
+def copy_kernel(request):
+    """Run every test with both paged-copy kernels (vectorised warp copy, TMA bulk pipeline)."""
+    from qwenedit_b200.paged import set_copy_mode
+
+    set_copy_mode(request.param)
+    yield request.param
+    set_copy_mode("auto")
+
+
 def _pool(L, H, D, tokens, dtype, page=1, extra=0, seed=0):
     elem = torch.empty((), dtype=dtype).element_size()
     budget = tokens * (L * 2 * H * D + extra) * elem
@@ -43,6 +53,7 @@ def test_gather_slots_bit_exact(L, H, D, dtype):
 @pytest.mark.parametrize("page", [4, 16, 64])
 def test_gather_through_block_table_bit_exact(page):
     pool = _pool(3, 24, 128, 64 * 40, torch.bfloat16, page=page, seed=page)
+    pool.index.shuffle_free(page)  # scattered pages: a real gather, not the contiguous-run view
     m = pool.match(np.arange(1, 10))
     assert m.length == 0
     n = page * 23 + page // 2  # a partial last page
