@@ -252,3 +252,38 @@ def test_one_k_edit_round_trip_property():
     pool.write(fresh, a)
     assert torch.equal(pool.gather(fresh), a)
     assert pool.device_errors() == 0
+
+
+def test_memory_pressure_data_matches_oracle():
+    """2K-session turns in a pool that holds two prefixes (LRU eviction every turn), 2 of the 60 layers:
+    after every turn each session's cached prefix gathers to exactly what the oracle pool holds."""
+    L, H, D, P = 2, 24, 128, 64
+    prefix = 16384 + 512
+    budget = (2 * prefix + 3 * P) * L * 2 * H * D * 2
+    ours = PagedKVPool("dit", L, H, D, budget, torch.bfloat16, DEV, page_size=P)
+    ref = RefPagedKVPool("dit", L, H, D, budget, torch.bfloat16, page_size=P)
+    ours.kv.zero_()
+    ref.kv.zero_()
+    rng = np.random.default_rng(5)
+    headers = [rng.integers(1, 1 << 62, size=512) for _ in range(4)]
+    for step in range(10):
+        s = step % 4
+        vids = np.concatenate([headers[s], rng.integers(1, 1 << 62, size=16384)])
+        for pool in (ours, ref):
+            m = pool.match(vids)
+            n = len(vids) - m.length
+            slots = pool.alloc(n)
+            assert slots is not None
+            new = _randn(100 + step, (L, 2, n, H, D)).bfloat16()
+            pool.write(slots, new.to(DEV) if pool is ours else new)
+            idx = torch.cat([m.indices.cpu(), slots.cpu()]) if m.length else slots.cpu()
+            pool.insert(vids, idx, owned_from=m.length)
+            m.release()
+        mo, mr = ours.match(vids), ref.match(vids)
+        assert mo.length == mr.length == prefix
+        assert torch.equal(ours.gather(mo.indices).cpu(), ref.gather(mr.indices))
+        mo.release()
+        mr.release()
+        assert ours.usage() == ref.usage()
+    assert ours.usage()["evicted_tokens"] > 0
+    assert ours.device_errors() == 0
