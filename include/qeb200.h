@@ -115,9 +115,15 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
                       const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S,
                       int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream);
 
-/* SiLU(gate) * value -> NVFP4   (fibo/fp4.py:83-91, wrapper :112-116). gate, value [M, K] bf16. */
+/* Fill `table` (65,536 uint16, 16-byte aligned device memory) with bf16(silu(g)) for every bf16 bit pattern g:
+ * bf16(g / (1 + exp(-g))) exactly as the fused kernel's arithmetic rounds it (fibo/fp4.py:90). Build it once
+ * per device; it is the workspace of qe_silu_mul_fp4. */
+int qe_silu_table_init(uint16_t *table, void *stream);
+
+/* SiLU(gate) * value -> NVFP4   (fibo/fp4.py:83-91, wrapper :112-116). gate, value [M, K] bf16; silu_table
+ * from qe_silu_table_init on the same device. q must be 8-byte aligned. */
 int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
-                    uint8_t *sf, void *stream);
+                    uint8_t *sf, const uint16_t *silu_table, void *stream);
 
 /* ---- prefix index: radix tree + slot allocator + LRU eviction (host) -------------------------
  *

@@ -187,6 +187,12 @@ int ref_norm_scale_fp4(const uint16_t *x, const uint16_t *w, const uint16_t *noi
   return 0;
 }
 
+/* bf16 bits of bf16(g / (1 + exp(-g))) for bf16 bits g (the SiLU value the silu_mul kernel multiplies). */
+uint16_t ref_silu_bf16(uint16_t g) {
+  float x = ref_bf16_to_f(g);
+  return ref_f_to_bf16(x / (1.0f + ref_exp(-x)));
+}
+
 /* Scratch: K floats. */
 int ref_silu_mul_fp4(const uint16_t *gate, const uint16_t *value, float gs, int64_t M, int64_t K, uint8_t *q,
                      uint8_t *sf, float *scratch) {

@@ -46,6 +46,8 @@ def lib() -> ctypes.CDLL:
         h.ref_e2m1.restype = c_uint8
         h.ref_f_to_bf16.argtypes = [c_float]
         h.ref_f_to_bf16.restype = c_uint16
+        h.ref_silu_bf16.argtypes = [c_uint16]
+        h.ref_silu_bf16.restype = c_uint16
         h.ref_pairwise_sum.argtypes = [POINTER(c_float), c_int64]
         h.ref_pairwise_sum.restype = c_float
         _lib = h

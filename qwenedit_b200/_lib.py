@@ -44,7 +44,8 @@ SIGNATURES: dict[str, list] = {
     "qe_append_slots_ptrs": [Planes, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     "qe_norm_scale_fp4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
-    "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
+    "qe_silu_table_init": [c_void_p, c_void_p],
     "qe_index_create": [c_int64, c_int32, POINTER(c_void_p)],
     "qe_index_destroy": [c_void_p],
     "qe_index_clear": [c_void_p],

@@ -69,6 +69,11 @@ __device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
   f32x2 r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
@@ -102,51 +107,72 @@ __device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
   asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-// two fp32 -> two e2m1 codes (round to nearest even on {0,.5,1,1.5,2,3,4,6}, saturating, sign in bit 3);
-// the low nibble holds the low element. These are exactly the reference's thresholds
-// {>0.25, >=0.75, >1.25, >=1.75, >2.5, >=3.5, >5}; the caller passes +0.0 for a -0.0 product.
-__device__ __forceinline__ uint32_t e2m1x2(f32x2 v) {
-  const float2 f = up2(v);
-  uint16_t r;
-  asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n cvt.u16.u8 %0, t;\n}\n"
-      : "=h"(r)
-      : "f"(f.y), "f"(f.x));
+// Four f32x2 pairs -> eight e2m1 codes in one word (pair i in byte i, its low element in the low nibble):
+// round to nearest even on {0, .5, 1, 1.5, 2, 3, 4, 6}, saturating, sign in bit 3. These are exactly the
+// reference's thresholds {>0.25, >=0.75, >1.25, >=1.75, >2.5, >=3.5, >5}; callers pass +0.0 for a -0.0
+// product (the reference's sign bit is `v < 0`).
+__device__ __forceinline__ uint32_t e2m1x8(f32x2 a, f32x2 b, f32x2 c, f32x2 d) {
+  const float2 fa = up2(a), fb = up2(b), fc = up2(c), fd = up2(d);
+  uint32_t r;
+  asm("{\n .reg .b8 t0, t1, t2, t3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 t0, %2, %1;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 t1, %4, %3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 t2, %6, %5;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 t3, %8, %7;\n"
+      " mov.b32 %0, {t0, t1, t2, t3};\n}\n"
+      : "=r"(r)
+      : "f"(fa.x), "f"(fa.y), "f"(fb.x), "f"(fb.y), "f"(fc.x), "f"(fc.y), "f"(fd.x), "f"(fd.y));
   return r;
 }
 
-// exp(x) within one ulp, for two lanes at once: Cody-Waite reduction with a two-constant ln 2 split,
-// degree-7 Taylor polynomial in Horner form with fused multiply-adds, exact 2^n rebuild in two factors.
-__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
-__device__ __forceinline__ f32x2 exp_cw2(f32x2 x2) {
-  const float2 x = up2(x2);
-  // n = rint(x * log2 e) by adding and removing 1.5 * 2^23 (round-to-nearest-even for |n| < 2^22, the range
-  // that matters); the integer n sits in the low mantissa bits of the biased sum
-  // (multiply, then add: the product is rounded to fp32 first, exactly as rintf(x * log2e) sees it)
-  const f32x2 biased = add2(mul2(x2, pk2(1.44269504088896341f, 1.44269504088896341f)),
-                            pk2(12582912.0f, 12582912.0f));
+// exp(-g) for SiLU's denominator, two lanes at once, within one ulp of exp: Cody-Waite reduction of x = -g
+// with a two-constant ln 2 split, degree-7 Taylor polynomial in Horner form with fused multiply-adds, then
+// p * 2^n as an exact p * 2^(n-1) times 2 (which overflows to +inf as exp does). Evaluated without
+// negating anything: with n from x and r' = -(x - n ln2) computed from g, Horner on r' with alternating-sign
+// coefficients yields (-1)^k times each Horner partial of the polynomial in r, so the result is bit for bit
+// p(r). g is first clamped to [-89, 80]: for x = -g above 88.7228 both give +inf, and below -17.4 exp(x) < 2^-25
+// so 1 + exp(x) rounds to 1 either way; the SiLU value is bit-identical to the unclamped exp with its special
+// cases (a NaN gate stays NaN through the division).
+__device__ __forceinline__ f32x2 exp_neg_silu2(f32x2 g2) {
+  float2 g = up2(g2);
+  g.x = fminf(fmaxf(g.x, -89.0f), 80.0f);
+  g.y = fminf(fmaxf(g.y, -89.0f), 80.0f);
+  g2 = pk2(g.x, g.y);
+  // biased = RN(RN(x log2 e) + 1.5 * 2^23) = 1.5 * 2^23 + rint(x log2 e), ties to even; x log2 e = -(g log2 e)
+  const f32x2 c2 = pk2(12582912.0f, 12582912.0f);
+  const f32x2 biased = sub2(c2, mul2(g2, pk2(1.44269504088896341f, 1.44269504088896341f)));
+  const f32x2 n2 = sub2(biased, c2);  // n, exactly
+  f32x2 rn = fma2(n2, pk2(0.693145751953125f, 0.693145751953125f), g2);  // -(x - n ln2_hi)
+  rn = fma2(n2, pk2(1.428606765330187045e-06f, 1.428606765330187045e-06f), rn);
+  f32x2 p = pk2(-1.98412698e-4f, -1.98412698e-4f);
+  p = fma2(p, rn, pk2(1.38888889e-3f, 1.38888889e-3f));
+  p = fma2(p, rn, pk2(-8.33333377e-3f, -8.33333377e-3f));
+  p = fma2(p, rn, pk2(4.16666679e-2f, 4.16666679e-2f));
+  p = fma2(p, rn, pk2(-1.66666672e-1f, -1.66666672e-1f));
+  p = fma2(p, rn, pk2(0.5f, 0.5f));
+  p = fma2(p, rn, pk2(-1.0f, -1.0f));
+  p = fma2(p, rn, pk2(1.0f, 1.0f));
+  // 2^(n-1) from the bits of biased (0x4b400000 + n): ((n - 1) + 127) << 23 == (bits << 23) + (126 << 23) mod 2^32
   const float2 bs = up2(biased);
-  const float2 nf = up2(add2(biased, pk2(-12582912.0f, -12582912.0f)));
-  const f32x2 nn = pk2(-nf.x, -nf.y);
-  f32x2 r = fma2(nn, pk2(0.693145751953125f, 0.693145751953125f), x2);
-  r = fma2(nn, pk2(1.428606765330187045e-06f, 1.428606765330187045e-06f), r);
-  f32x2 p = pk2(1.98412698e-4f, 1.98412698e-4f);
-  p = fma2(p, r, pk2(1.38888889e-3f, 1.38888889e-3f));
-  p = fma2(p, r, pk2(8.33333377e-3f, 8.33333377e-3f));
-  p = fma2(p, r, pk2(4.16666679e-2f, 4.16666679e-2f));
-  p = fma2(p, r, pk2(1.66666672e-1f, 1.66666672e-1f));
-  p = fma2(p, r, pk2(0.5f, 0.5f));
-  p = fma2(p, r, pk2(1.0f, 1.0f));
-  p = fma2(p, r, pk2(1.0f, 1.0f));
-  const int ix = __float_as_int(bs.x) - 0x4b400000, iy = __float_as_int(bs.y) - 0x4b400000;
-  const int ax = ix >> 1, ay = iy >> 1;
-  const float2 e = up2(mul2(mul2(p, pk2(pow2i(ax), pow2i(ay))), pk2(pow2i(ix - ax), pow2i(iy - ay))));
-  float ox = e.x, oy = e.y;
-  if (!(x.x <= 88.72283935546875f)) ox = x.x != x.x ? x.x : __int_as_float(0x7f800000);
-  if (x.x < -103.97208404541015625f) ox = 0.0f;
-  if (!(x.y <= 88.72283935546875f)) oy = x.y != x.y ? x.y : __int_as_float(0x7f800000);
-  if (x.y < -103.97208404541015625f) oy = 0.0f;
-  return pk2(ox, oy);
+  const f32x2 half_scale = pk2(__uint_as_float((__float_as_uint(bs.x) << 23) + (126u << 23)),
+                               __uint_as_float((__float_as_uint(bs.y) << 23) + (126u << 23)));
+  return mul2(mul2(p, half_scale), pk2(2.0f, 2.0f));
+}
+
+// RN(a / b) rounded on to bf16, for b >= 1: a reciprocal-estimate quotient is within a few ulps of the
+// correctly rounded one, so it rounds to the same bf16 unless it sits within 8 ulps of a bf16 midpoint (or
+// b is huge); those rare cases take the IEEE division.
+__device__ __forceinline__ float div_for_bf16(float a, float b) {
+  const float q = __fmul_rn(a, rcp_approx(b));
+  const uint32_t low = __float_as_uint(q) & 0xffffu;
+  if (low - 0x7ff8u <= 16u || !(b < 1.2676506e30f)) return __fdiv_rn(a, b);  // 2^100
+  return q;
 }
 
 // Byte offset of the e4m3 scale of (row m, group g) in the 128x4-swizzled layout (fibo/fp4.py:59-60).
@@ -168,10 +194,10 @@ __device__ __forceinline__ uint2 quantize16(const uint32_t (&y)[8], float gs, fl
   const float sff = e4m3_value(sb);
   const float scale = sff != 0.0f ? __frcp_rn(__fmul_rn(sff, inv_gs)) : 0.0f;
   const f32x2 scale2 = pk2(scale, scale), zero2 = pk2(0.0f, 0.0f);
-  uint32_t c[8];
+  f32x2 v[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = e2m1x2(fma2(bf2_f2(y[i]), scale2, zero2));
-  return make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24), c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
+  for (int i = 0; i < 8; ++i) v[i] = fma2(bf2_f2(y[i]), scale2, zero2);
+  return make_uint2(e2m1x8(v[0], v[1], v[2], v[3]), e2m1x8(v[4], v[5], v[6], v[7]));
 }
 
 __device__ __forceinline__ void unpack16(const uint4 &a, const uint4 &b, uint32_t (&w)[8]) {
@@ -233,51 +259,53 @@ __device__ __forceinline__ void load_mod8(const __nv_bfloat16 *row, int64_t col,
   }
 }
 
-constexpr int kMaxRegGroups = 8;  // rows up to K = 4096 stay in registers between the two passes
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(
+                   smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-// One warp per row. Lane l owns the 16-value groups g = l + 32 i of the row (two 16-byte chunks each):
-// pass 1 loads them (1 KiB of the row per warp instruction pair) and stages them in leaf-major shared memory
-// for the ordered sum of squares; pass 2 quantises each group from registers (K <= 4096) or shared memory.
-template <int kWarps, bool kRegs>
+// One warp per row, rows strided over the grid. Each warp owns two row buffers in shared memory: while it
+// quantises row m from one, cp.async streams its next row into the other (no registers held for the
+// prefetch). Rows are stored leaf-major with an XOR swizzle so the ordered sum of squares (one leaf per
+// lane) and the coalesced fill are both free of bank conflicts. In the element-wise pass lane l owns the
+// 16-value groups g = l + 32 i (two 16-byte chunks each).
+template <int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams p) {
   extern __shared__ uint4 smem[];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
-  const int gpr = int(p.K >> 4);           // 16-value groups per row
-  const int gpl = (gpr + 31) >> 5;         // groups per lane
-  uint4 *row_s = smem + int64_t(wid) * p.row_chunks;
+  const int gpr = int(p.K >> 4);  // 16-value groups per row
+  uint4 *bufs = smem + int64_t(wid) * 2 * p.row_chunks;
   const int64_t warp0 = int64_t(blockIdx.x) * kWarps + wid;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
   const float gs = __ldg(p.gs);
   const float inv_gs = __fdiv_rn(1.0f, gs);
   const float kf = float(p.K);
 
-  for (int64_t m = warp0; m < p.padded; m += nwarps) {
-    if (m >= p.M) {
+  auto fetch = [&](int64_t row, uint4 *dst) {  // issue the async copy of one row (no-op past M)
+    if (row < p.M) {
+      const uint4 *src = p.x + row * (p.K >> 3);
+      for (int c = lane; c < 2 * gpr; c += 32) cp_async16(dst + swz(c), src + c);
+    }
+    cp_async_commit();
+  };
+
+  fetch(warp0, bufs);
+  int cur = 0;
+  for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1) {
+    fetch(m + nwarps, bufs + (cur ^ 1) * p.row_chunks);
+    cp_async_wait_1();  // this row's copies (all but the newest group) have landed
+    __syncwarp();
+    if (m >= p.M) {  // padding rows of the last 128-row tile: zero scales, no codes
       zero_sf_row(p.sf, m, p.K, lane);
+      __syncwarp();
       continue;
     }
-    const uint4 *xr = p.x + m * (p.K >> 3);
-    uint4 xa[kRegs ? kMaxRegGroups : 1], xb[kRegs ? kMaxRegGroups : 1];
-#pragma unroll
-    for (int i = 0; i < (kRegs ? kMaxRegGroups : 1); ++i) {
-      if (kRegs && i < gpl) {
-        const int g = lane + 32 * i;
-        if (g < gpr) {
-          xa[i] = ld16(xr + 2 * g);
-          xb[i] = ld16(xr + 2 * g + 1);
-          row_s[swz(2 * g)] = xa[i];
-          row_s[swz(2 * g + 1)] = xb[i];
-        }
-      }
-    }
-    if (!kRegs) {
-      for (int g = lane; g < gpr; g += 32) {
-        row_s[swz(2 * g)] = ld16(xr + 2 * g);
-        row_s[swz(2 * g + 1)] = ld16(xr + 2 * g + 1);
-      }
-    }
-    __syncwarp();
+    const uint4 *row_s = bufs + cur * p.row_chunks;
 
     // sum of squares, numpy pairwise order: leaf j = elements [leaf_len*j, leaf_len*j + leaf_len); lane l
     // owns leaves l, l+32, l+64, l+96; each round's 32 leaves reduce by a butterfly (a balanced tree), and
@@ -309,7 +337,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const f32x2 f = bf2_f2(u[i]);
-              acc[i] = add2(acc[i], mul2(f, f));
+              acc[i] = fma2(f, f, acc[i]);  // f * f is exact for bf16 f: same as rounding, then adding
             }
           }
           // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7))
@@ -337,9 +365,11 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     const __nv_bfloat16 *sh_row = sh_base ? sh_base + b * p.mod_stride : nullptr;
     uint8_t *q_row = p.q + m * (p.K >> 1);
 
-    auto group = [&](int g, const uint4 &x0, const uint4 &x1) {
+    // scale-byte offset = row part + group part (fibo/fp4.py:60)
+    const int64_t sf_row = (m >> 7) * (p.K / 64 * 512) + (m & 31) * 16 + ((m & 127) >> 5) * 4;
+    auto group = [&](int g) {
       uint32_t xu[8], wu[8], mv[8], sv[8];
-      unpack16(x0, x1, xu);
+      unpack16(row_s[swz(2 * g)], row_s[swz(2 * g + 1)], xu);
       unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), wu);
       load_mod8(mod_row, int64_t(g) * 16, p.mods_vec, mv);
       load_mod8(mod_row, int64_t(g) * 16 + 8, p.mods_vec, mv + 4);
@@ -359,38 +389,63 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
       }
       uint32_t sb;
       const uint2 codes = quantize16(y, gs, inv_gs, sb);
-      *reinterpret_cast<uint2 *>(q_row + int64_t(g) * 8) = codes;
-      p.sf[sf_offset(m, g, p.K)] = uint8_t(sb);
+      *reinterpret_cast<uint2 *>(q_row + g * 8) = codes;
+      p.sf[sf_row + (g >> 2) * 512 + (g & 3)] = uint8_t(sb);
     };
-    if (kRegs) {
-#pragma unroll
-      for (int i = 0; i < kMaxRegGroups; ++i) {
-        const int g = lane + 32 * i;
-        if (i < gpl && g < gpr) group(g, xa[i], xb[i]);
-      }
-    } else {
-      for (int g = lane; g < gpr; g += 32) group(g, row_s[swz(2 * g)], row_s[swz(2 * g + 1)]);
+    int g = lane;
+    for (; g + 32 < gpr; g += 64) {  // two independent groups per iteration
+      group(g);
+      group(g + 32);
     }
-    __syncwarp();
+    if (g < gpr) group(g);
+    __syncwarp();  // every lane is done with this buffer before it is refilled
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---- SiLU(gate) * value -> NVFP4 ---------------------------------------------------------------
+// bf16(silu(g)) depends on the 16 bits of g alone, so it is a 65,536-entry table, computed once per device
+// by silu_table_kernel with the exact arithmetic below (Cody-Waite exp, IEEE-rounded quotient) and staged
+// in shared memory by each CTA of silu_mul_fp4_kernel: per element the SiLU costs one shared-memory load.
+constexpr int kSiluTable = 65536;
+
+// bf16 bits of bf16(g / (1 + exp(-g))) for the two bf16 values of word w
+__device__ __forceinline__ uint32_t silu_bf16x2(uint32_t w) {
+  const f32x2 g2 = bf2_f2(w);
+  const float2 g = up2(g2);
+  const float2 d = up2(add2(pk2(1.0f, 1.0f), exp_neg_silu2(g2)));
+  return f2_bf2(pk2(div_for_bf16(g.x, d.x), div_for_bf16(g.y, d.y)));
+}
+
+__global__ void __launch_bounds__(256) silu_table_kernel(uint32_t *table) {
+  const uint32_t i = blockIdx.x * 256 + threadIdx.x;  // one word = entries 2i, 2i+1
+  if (i < kSiluTable / 2) table[i] = silu_bf16x2((2 * i) | ((2 * i + 1) << 16));
+}
+
 struct SiluParams {
   const uint4 *gate;
   const uint4 *value;
   const float *gs;
+  const uint4 *table;  // kSiluTable bf16 entries
   uint8_t *q;
   uint8_t *sf;
   int64_t M, K, padded;
 };
 
-constexpr int kSiluThreads = 256;
-constexpr int kSiluItems = 2;  // warp items (32 groups each) in flight per iteration
+constexpr int kSiluThreads = 1024;  // one CTA per SM (the table takes 128 KiB of shared memory)
+constexpr int kSiluItems = 2;       // warp items (32 groups each) in flight per iteration
+
+__device__ __forceinline__ uint32_t silu_lookup(const uint16_t *tab, uint32_t w) {
+  return uint32_t(tab[w & 0xffffu]) | (uint32_t(tab[w >> 16]) << 16);
+}
 
 // A warp item is 32 consecutive 16-value groups of one row, one group per lane; kSiluItems items per
 // iteration so every lane has 8 16-byte loads in flight before it computes.
-__global__ void __launch_bounds__(kSiluThreads, 2) silu_mul_fp4_kernel(SiluParams p) {
+__global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
+  extern __shared__ uint4 tab4[];
+  for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
+  __syncthreads();
+  const uint16_t *tab = reinterpret_cast<const uint16_t *>(tab4);
   const int lane = threadIdx.x & 31;
   const int gpr = int(p.K >> 4);
   const int segs = (gpr + 31) >> 5;
@@ -425,13 +480,7 @@ __global__ void __launch_bounds__(kSiluThreads, 2) silu_mul_fp4_kernel(SiluParam
       unpack16(ga[u], gb[u], gw);
       unpack16(va[u], vb[u], vw);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        // bf16(bf16(g / (1 + exp(-g))) * v)
-        const f32x2 g2 = bf2_f2(gw[i]);
-        const float2 g = up2(g2);
-        const float2 d = up2(add2(pk2(1.0f, 1.0f), exp_cw2(pk2(-g.x, -g.y))));
-        y[i] = bmul2(f2_bf2(pk2(__fdiv_rn(g.x, d.x), __fdiv_rn(g.y, d.y))), vw[i]);
-      }
+      for (int i = 0; i < 8; ++i) y[i] = bmul2(silu_lookup(tab, gw[i]), vw[i]);  // bf16(silu(g) * v)
       uint32_t sb;
       const uint2 codes = quantize16(y, gs, inv_gs, sb);
       *reinterpret_cast<uint2 *>(p.q + row[u] * (p.K >> 1) + int64_t(grp[u]) * 8) = codes;
@@ -472,6 +521,7 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
                                              (long long)M, (long long)S, (long long)K);
   if (K % 64 != 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K=%lld must be a multiple of 64", (long long)K);
   if (K > 16384) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K=%lld above the supported 16384", (long long)K);
+  if (!qe::aligned16(x)) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: x must be 16-byte aligned");
   if (M % S != 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: M=%lld is not a multiple of S=%lld",
                                (long long)M, (long long)S);
   if (mod_stride < 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: negative mod_stride");
@@ -505,21 +555,20 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   for (const void *ptr : {noisy, clean, shift, shift_clean})
     if (ptr && !qe::aligned16(ptr)) vec = false;
   p.mods_vec = vec ? 1 : 0;
-  // shared memory: one staged row per warp in whole 256-byte leaves (the swizzle stays inside a leaf)
+  // shared memory: two row buffers per warp, each in whole 256-byte leaves (the swizzle stays inside a leaf)
   p.row_chunks = int32_t((K + 127) / 128 * 16);
-  const size_t per_warp = size_t(p.row_chunks) * 16;
+  const size_t per_warp = 2 * size_t(p.row_chunks) * 16;
   constexpr size_t kSmemMax = 227 * 1024;
-  const int warps = per_warp * 8 <= kSmemMax ? 8 : 4;
+  const int warps = per_warp * 8 <= kSmemMax ? 8 : per_warp * 4 <= kSmemMax ? 4 : 2;
   const size_t smem = per_warp * size_t(warps);
-  if (smem > kSmemMax) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for one row per warp");
+  if (smem > kSmemMax) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for two rows per warp");
   // the shared-memory opt-in is per device context: remember it per device
-  static bool attr_set[64][4] = {};
+  static bool attr_set[64][3] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  const bool regs = K <= 16 * 32 * qe::kMaxRegGroups;
-  auto kernel = warps == 8 ? (regs ? qe::norm_scale_fp4_kernel<8, true> : qe::norm_scale_fp4_kernel<8, false>)
-                           : (regs ? qe::norm_scale_fp4_kernel<4, true> : qe::norm_scale_fp4_kernel<4, false>);
-  const int variant = (warps == 8 ? 2 : 0) + (regs ? 1 : 0);
+  auto kernel = warps == 8 ? qe::norm_scale_fp4_kernel<8>
+                           : warps == 4 ? qe::norm_scale_fp4_kernel<4> : qe::norm_scale_fp4_kernel<2>;
+  const int variant = warps == 8 ? 2 : warps == 4 ? 1 : 0;
   if (!attr_set[dev][variant]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemMax));
     if (e != cudaSuccess) return qe::cuda_status(e, "qe_norm_scale_fp4: smem attribute");
@@ -534,35 +583,51 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   return s ? s : qe::ok();
 }
 
+int qe_silu_table_init(uint16_t *table, void *stream) {
+  if (!table) return fail(QE_ERR_INVALID, "qe_silu_table_init: null table");
+  if (!qe::aligned16(table)) return fail(QE_ERR_INVALID, "qe_silu_table_init: table must be 16-byte aligned");
+  qe::silu_table_kernel<<<dim3(qe::kSiluTable / 2 / 256), dim3(256), 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<uint32_t *>(table));
+  int s = qe::cuda_status(cudaGetLastError(), "qe_silu_table_init launch");
+  return s ? s : qe::ok();
+}
+
 int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
-                    uint8_t *sf, void *stream) {
-  if (!gate || !value || !gs || !q || !sf) return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: null argument");
+                    uint8_t *sf, const uint16_t *silu_table, void *stream) {
+  if (!gate || !value || !gs || !q || !sf || !silu_table)
+    return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: null argument");
   if (M < 0 || K <= 0) return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: bad sizes");
   if (K % 64 != 0) return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: K=%lld must be a multiple of 64", (long long)K);
-  if (!qe::aligned16(gate) || !qe::aligned16(value))
-    return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: gate and value must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(sf) & 3))
-    return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: q and sf must be 4-byte aligned");
+  if (!qe::aligned16(gate) || !qe::aligned16(value) || !qe::aligned16(silu_table))
+    return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: gate, value and the table must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(q) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3))
+    return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: q must be 8-byte and sf 4-byte aligned");
   const int64_t padded = qe::pad128(M);
   if (padded == 0) return qe::ok();
   qe::SiluParams p{};
   p.gate = static_cast<const uint4 *>(gate);
   p.value = static_cast<const uint4 *>(value);
   p.gs = gs;
+  p.table = reinterpret_cast<const uint4 *>(silu_table);
   p.q = q;
   p.sf = sf;
   p.M = M;
   p.K = K;
   p.padded = padded;
+  constexpr size_t smem = size_t(qe::kSiluTable) * 2;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(qe::silu_mul_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return qe::cuda_status(e, "qe_silu_mul_fp4: smem attribute");
+    attr_set[dev] = true;
+  }
   const int64_t items = M * ((K / 16 + 31) / 32);  // warp items: 32 groups of one row
   const int64_t warps_per_block = qe::kSiluThreads / 32;
   int64_t blocks = (std::max<int64_t>(items, (padded - M) * (K / 64) / 32) + warps_per_block - 1) / warps_per_block;
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qe::silu_mul_fp4_kernel, qe::kSiluThreads, 0) != cudaSuccess ||
-      occ < 1)
-    occ = 2;
-  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(qe::sm_count()) * occ));
-  qe::silu_mul_fp4_kernel<<<dim3(unsigned(blocks)), dim3(qe::kSiluThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
+  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(qe::sm_count())));
+  qe::silu_mul_fp4_kernel<<<dim3(unsigned(blocks)), dim3(qe::kSiluThreads), smem, static_cast<cudaStream_t>(stream)>>>(p);
   int s = qe::cuda_status(cudaGetLastError(), "qe_silu_mul_fp4 launch");
   return s ? s : qe::ok();
 }

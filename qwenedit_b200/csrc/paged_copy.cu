@@ -233,8 +233,7 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
     const uint32_t rb = uint32_t(p.row_bytes);
     uint32_t moved = 0;
     // the contiguous side (gather: output rows t0..; append: source rows t0..) is one op
-    const bool contiguous_side_is_load = !kGather;
-    if (kLoad == contiguous_side_is_load) {
+    if constexpr (kLoad == !kGather) {  // the contiguous side
       char *oth_ptr = oth_plane + t0 * p.row_bytes;
       if (kLoad) {
         bulk_load(stage, oth_ptr, uint32_t(rows) * rb, bar);
@@ -242,7 +241,7 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
         bulk_store(oth_ptr, stage, uint32_t(rows) * rb);
       }
       return uint32_t(rows) * rb;
-    }
+    } else {
     for (int64_t i = 0; i < rows; ++i) {
       const int64_t slot = __ldg(p.slots + t0 + i);
       if (slot < 0 || slot >= p.pool_rows) {
@@ -258,6 +257,7 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
       moved += rb;
     }
     return moved;
+    }
   }
 }
 

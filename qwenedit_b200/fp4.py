@@ -114,6 +114,22 @@ def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clea
     return Quantized(q, sf, x.shape)
 
 
+_silu_tables: dict[int, torch.Tensor] = {}
+
+
+def silu_table(device) -> torch.Tensor:
+    """Per-device table of bf16(silu(g)) for all 65,536 bf16 g (128 KiB), built once by ``qe_silu_table_init``."""
+    device = torch.device(device)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    table = _silu_tables.get(index)
+    if table is None:
+        table = torch.empty(65536, dtype=torch.int16, device=torch.device("cuda", index))
+        with torch.cuda.device(index):
+            _lib.call("qe_silu_table_init", table.data_ptr(), torch.cuda.current_stream(index).cuda_stream)
+        _silu_tables[index] = table
+    return table
+
+
 def silu_mul_fp4(gate, value, gs, block=1024) -> Quantized:
     """``silu(gate) * value`` quantised to NVFP4 (``block`` is accepted for signature parity and unused)."""
     _check_cuda_bf16("gate", gate)
@@ -127,7 +143,11 @@ def silu_mul_fp4(gate, value, gs, block=1024) -> Quantized:
         raise ValueError(f"K={k} must be a multiple of 64")
     m, padded, q, sf = _buffers(gate, k)
     gs = _gs(gs, gate.device)
+    table = silu_table(gate.device)
     with torch.cuda.device(gate.device):
+        stream = torch.cuda.current_stream(gate.device)
+        if table.device != gate.device:
+            raise ValueError("silu table on another device")
         _lib.call("qe_silu_mul_fp4", gate.data_ptr(), value.data_ptr(), gs.data_ptr(), m, k, q.data_ptr(),
-                  sf.data_ptr(), torch.cuda.current_stream(gate.device).cuda_stream)
+                  sf.data_ptr(), table.data_ptr(), stream.cuda_stream)
     return Quantized(q, sf, gate.shape)

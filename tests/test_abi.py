@@ -42,6 +42,6 @@ def test_invalid_arguments_raise_not_abort():
         _lib.call("qe_index_create", 16, 0, ctypes.byref(ctypes.c_void_p()))
     # device entry points validate before touching the GPU
     with pytest.raises(ValueError, match="multiple of 64"):
-        _lib.call("qe_silu_mul_fp4", 16, 16, 16, 4, 100, 16, 16, None)
+        _lib.call("qe_silu_mul_fp4", 16, 16, 16, 4, 100, 16, 16, 16, None)
     with pytest.raises(ValueError, match="null"):
         _lib.call("qe_gather_slots", _lib.planes(0, 0, 0, 2), 10, _lib.planes(16, 0, 0, 2), 2, 64, 0, 4, None, None)

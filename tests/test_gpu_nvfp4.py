@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from oracle import nvfp4_ref
-from qwenedit_b200.fp4 import Quantized, norm_scale_fp4, silu_mul_fp4
+from qwenedit_b200.fp4 import Quantized, norm_scale_fp4, silu_mul_fp4, silu_table
 from tests.golden import cases, inputs
 
 pytestmark = pytest.mark.gpu
@@ -125,3 +125,18 @@ def test_argument_errors():
         silu_mul_fp4(torch.zeros(4, 64, device=DEV), torch.zeros(4, 64, device=DEV), _gs(1.0))
     with pytest.raises(RuntimeError, match="CUDA"):
         silu_mul_fp4(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, 64, dtype=torch.bfloat16), _gs(1.0))
+
+
+def test_silu_table_is_exact_for_every_bf16_input():
+    """The SiLU table (one entry per bf16 bit pattern) equals the oracle's bf16(g / (1 + exp(-g))) for all 65,536
+    inputs; NaN inputs (and -inf, which gives inf/inf) map to a NaN on both sides."""
+    table = silu_table(DEV).cpu().numpy().view(np.uint16)
+    ref = np.array([nvfp4_ref.lib().ref_silu_bf16(i) for i in range(65536)], np.uint16)
+    g = np.arange(65536, dtype=np.uint32)
+    nan_in = ((g & 0x7F80) == 0x7F80) & ((g & 0x7F) != 0)
+    neg_inf = g == 0xFF80
+    def is_nan(bits):
+        return ((bits & 0x7F80) == 0x7F80) & ((bits & 0x7F) != 0)
+    special = nan_in | neg_inf
+    assert is_nan(table[special]).all() and is_nan(ref[special]).all()
+    np.testing.assert_array_equal(table[~special], ref[~special])
