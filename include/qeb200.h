@@ -90,6 +90,21 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
                          int64_t row_bytes, const int64_t *slots, int64_t n_tokens, int32_t *err_flag,
                          void *stream);
 
+/* qe_append_slots_ptrs for callers that cannot allocate device memory: the per-plane source pointers are
+ * passed as a HOST array and copied into a table inside this library's own device memory, so the caller
+ * allocates nothing (qe_append_slots_ptrs needs a caller-allocated device array of pointers). Meant for hosts
+ * whose device memory is all owned by another allocator (e.g. a serving process that reserved the GPU's memory
+ * up front), or code paths that must not allocate. No counterpart in the reference.
+ * Limits: n_planes <= 1024 (an 8 KiB table per GPU that loads the library, held until exit); larger calls fail
+ * with QE_ERR_INVALID before any work. The first call on each device looks the table up with
+ * cudaGetSymbolAddress, so make that first call before any stream capture. Every call rewrites the table's
+ * first n_planes entries on `stream` and the kernel reads them from there: calls whose work can overlap on the
+ * GPU (different streams) race on the shared table; issue them on one stream. Allocates nothing: no cudaMalloc,
+ * cudaFree or allocating library call; the host array may be reused once the call returns. */
+int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs_host,
+                                 int32_t n_planes, int64_t row_bytes, const int64_t *slots, int64_t n_tokens,
+                                 int32_t *err_flag, void *stream);
+
 /* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel,
  * 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned rows of <= 32 KiB,
  * else the warp kernel). No counterpart in the reference; for measurement and tuning. */

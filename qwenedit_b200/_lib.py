@@ -42,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "qe_append_slots": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     "qe_append_pages": [Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_void_p],
     "qe_append_slots_ptrs": [Planes, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    "qe_append_slots_ptrs_noalloc": [Planes, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p,
+                                     c_void_p],
     "qe_norm_scale_fp4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
     "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],

@@ -549,3 +549,67 @@ int qe_set_paged_copy_mode(int32_t mode) {
 const char *qe_version(void) { return "qeb200 0.1.0 (sm_100a)"; }
 
 }  // extern "C"
+
+// ---- variant of qe_append_slots_ptrs that allocates nothing ----------------------------------------
+// The per-plane source-pointer table lives in this module's own device memory: a file-scope array that
+// every GPU loading the library holds until exit. Host code must not pass the array's name to a kernel (in
+// host code it is only a stand-in symbol); its device address comes from cudaGetSymbolAddress, taken once
+// per device with that device current.
+namespace qe {
+constexpr int32_t kStaticMaxPlanes = 1024;  // 8 KiB of pointers: 512 layers of K and V
+}  // namespace qe
+
+static __device__ __align__(256) const void *g_static_src_ptrs[qe::kStaticMaxPlanes];
+
+namespace qe {
+namespace {
+int static_ptr_table(const void *const **out) {
+  static const void *const *addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "qe_append_slots_ptrs_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: device %d above 63", dev);
+  if (!addr[dev]) {
+    void *ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_src_ptrs);
+    if (e != cudaSuccess) return cuda_status(e, "qe_append_slots_ptrs_noalloc: cudaGetSymbolAddress");
+    addr[dev] = static_cast<const void *const *>(ptr);
+  }
+  *out = addr[dev];
+  return QE_OK;
+}
+}  // namespace
+}  // namespace qe
+
+extern "C" int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs_host,
+                                            int32_t n_planes, int64_t row_bytes, const int64_t *slots,
+                                            int64_t n_tokens, int32_t *err_flag, void *stream) {
+  int s = qe::common_checks("qe_append_slots_ptrs_noalloc", pool, pool_rows, n_planes, row_bytes, n_tokens);
+  if (s) return s;
+  if (n_planes > qe::kStaticMaxPlanes)
+    return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: %d planes exceed the static table's %d", n_planes,
+                qe::kStaticMaxPlanes);
+  if (n_planes == 0 || n_tokens == 0) return qe::ok();
+  if (!src_ptrs_host || !slots) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: null source pointers or slots");
+  const void *const *table = nullptr;
+  s = qe::static_ptr_table(&table);
+  if (s) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the table is written on the caller's stream ahead of the kernel that reads it; the host array may be
+  // reused as soon as this call returns
+  s = qe::cuda_status(cudaMemcpyAsync(const_cast<const void **>(table), src_ptrs_host, size_t(n_planes) * sizeof(void *),
+                                      cudaMemcpyHostToDevice, st),
+                      "qe_append_slots_ptrs_noalloc: pointer table copy");
+  if (s) return s;
+  qe::CopyParams p{};
+  p.pool = qe::to_planes(pool);
+  p.other_ptrs = table;
+  p.pool_rows = pool_rows;
+  p.n_tokens = n_tokens;
+  p.row_bytes = row_bytes;
+  p.slots = slots;
+  p.n_planes = n_planes;
+  p.err = err_flag;
+  s = qe::launch<qe::kSlots, false, true>(p, qe::align_of(pool, nullptr, row_bytes), st);
+  return s ? s : qe::ok();
+}
