@@ -20,6 +20,7 @@
 // one shuffle, each lane packs its 8 codes into a 32-bit store, and each quad of groups (one row, four
 // consecutive scales) is written as one 32-bit store.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstdint>
@@ -37,12 +38,13 @@ __device__ __forceinline__ uint32_t e4m3_byte(float v) {
   return uint32_t(out) & 0xffu;
 }
 
-// exact value of an e4m3 byte (bias 7, subnormals at exponent field 0, 0x7f/0xff = NaN)
+// exact value of an e4m3 byte (every e4m3 value, NaN included, is an f16 value): the byte is placed in both
+// halves so the result does not depend on which half the conversion reads
 __device__ __forceinline__ float e4m3_value(uint32_t byte) {
-  const uint32_t e = (byte >> 3) & 15u, m = byte & 7u;
-  if (e == 15u && m == 7u) return __int_as_float(0x7fc00000);
-  const float mag = e == 0u ? float(m) * 0.001953125f : float(8u + m) * __int_as_float(int(e + 117u) << 23);
-  return (byte & 0x80u) ? -mag : mag;
+  const uint16_t pair = uint16_t(byte | (byte << 8));
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(pair));
+  return __half2float(__ushort_as_half(uint16_t(h2 & 0xffffu)));
 }
 
 // ---- packed arithmetic (Blackwell f32x2 / bf16x2) ----------------------------------------------
@@ -234,15 +236,23 @@ struct NormParams {
   int32_t leaves;      // P / 128 leaves (P = next_pow2(K) >= 128), or 1 when P == 64
   int32_t leaf_len;    // 128, or 64 when P == 64
   int32_t mods_vec;    // mod / shift rows are 16-byte aligned
-  int32_t row_chunks;  // 16-byte chunks of shared memory per warp (whole 256-byte leaves)
+  int32_t row_chunks;  // 16-byte chunks of one row buffer (whole 256-byte leaves)
+  int32_t batches;     // modulation rows staged per variant
+  int32_t variants;    // 1, or 2 with a token mask (noisy, clean)
   float eps;
 };
 
-// smem chunk index of 16-byte chunk c of a row: leaf-major, XOR swizzle on the chunk within its leaf
+// Shared-memory chunk of 16-byte chunk c of a row: leaf-major with an XOR swizzle inside the leaf, chosen so
+// the three access patterns are free of bank conflicts: the coalesced fill (8 consecutive chunks), the
+// ordered reduction (lane j walks leaf j) and the per-group reads (lane l takes chunks 2l and 2l+1).
 __device__ __forceinline__ int swz(int c) {
   const int leaf = c >> 4;
-  return (leaf << 4) | ((c & 15) ^ (leaf & 15));
+  return (leaf << 4) | ((c & 15) ^ (leaf & 15) ^ ((c >> 3) & 1));
 }
+
+// Per-column constant rows (w, bf16(1 + scale), shift) are stored group-interleaved: the two chunks of group
+// g at g and half + g, so the per-group reads of a quarter warp hit 8 different bank groups.
+__device__ __forceinline__ int gix(int c, int half) { return (c & 1) ? half + (c >> 1) : (c >> 1); }
 
 // 8 bf16 modulation values starting at `col` as 4 bf16x2 words
 __device__ __forceinline__ void load_mod8(const __nv_bfloat16 *row, int64_t col, bool vec, uint32_t *out) {
@@ -268,18 +278,30 @@ __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
+// Bytes of the per-CTA constant tables: w, then (batches x variants) rows of bf16(1 + scale), then as many
+// shift rows when there is a shift.
+inline size_t norm_table_bytes(int64_t K, int64_t rows, bool shift) {
+  return size_t(K) * 2 * size_t(1 + rows * (shift ? 2 : 1));
+}
+
 // One warp per row, rows strided over the grid. Each warp owns two row buffers in shared memory: while it
-// quantises row m from one, cp.async streams its next row into the other (no registers held for the
-// prefetch). Rows are stored leaf-major with an XOR swizzle so the ordered sum of squares (one leaf per
-// lane) and the coalesced fill are both free of bank conflicts. In the element-wise pass lane l owns the
-// 16-value groups g = l + 32 i (two 16-byte chunks each).
-template <int kWarps>
+// quantises row m from one, cp.async streams its next row into the other. With kTables the CTA first stages
+// the per-column constants (w, the pre-rounded bf16(1 + scale) rows of every batch and mask variant, the
+// shift rows) in shared memory, so the per-row work reads them from there; without, they come from global
+// memory. In the element-wise pass lane l owns the 16-value groups g = l + 32 i.
+template <int kWarps, bool kTables, bool kShift>
 __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams p) {
   extern __shared__ uint4 smem[];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
   const int gpr = int(p.K >> 4);  // 16-value groups per row
-  uint4 *bufs = smem + int64_t(wid) * 2 * p.row_chunks;
+  const int kc = int(p.K >> 3);   // 16-byte chunks per row
+  const int half = gpr;           // group-interleaved table: second chunks start here
+  const int mod_rows = p.batches * p.variants;
+  uint4 *w_s = smem;
+  uint4 *m1_s = w_s + (kTables ? kc : 0);
+  uint4 *sh_s = m1_s + (kTables ? kc * mod_rows : 0);
+  uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + int64_t(wid) * 2 * p.row_chunks;
   const int64_t warp0 = int64_t(blockIdx.x) * kWarps + wid;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
   const float gs = __ldg(p.gs);
@@ -289,12 +311,34 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   auto fetch = [&](int64_t row, uint4 *dst) {  // issue the async copy of one row (no-op past M)
     if (row < p.M) {
       const uint4 *src = p.x + row * (p.K >> 3);
-      for (int c = lane; c < 2 * gpr; c += 32) cp_async16(dst + swz(c), src + c);
+      for (int c = lane; c < kc; c += 32) cp_async16(dst + swz(c), src + c);
     }
     cp_async_commit();
   };
-
   fetch(warp0, bufs);
+
+  if (kTables) {
+    for (int c = threadIdx.x; c < kc; c += kWarps * 32) w_s[gix(c, half)] = __ldg(p.w + c);
+    for (int t = 0; t < mod_rows; ++t) {
+      const int64_t b = t / p.variants;
+      const bool noisy = (t % p.variants) == 0;
+      const __nv_bfloat16 *mrow = (noisy ? p.noisy : p.clean) + b * p.mod_stride;
+      const __nv_bfloat16 *srow = kShift ? (noisy ? p.shift : p.shift_clean) + b * p.mod_stride : nullptr;
+      for (int c = threadIdx.x; c < kc; c += kWarps * 32) {
+        uint32_t mv[4];
+        load_mod8(mrow, int64_t(c) * 8, p.mods_vec, mv);
+        m1_s[t * kc + gix(c, half)] =
+            make_uint4(badd2(kOne2, mv[0]), badd2(kOne2, mv[1]), badd2(kOne2, mv[2]), badd2(kOne2, mv[3]));
+        if (kShift) {
+          uint32_t sv[4];
+          load_mod8(srow, int64_t(c) * 8, p.mods_vec, sv);
+          sh_s[t * kc + gix(c, half)] = make_uint4(sv[0], sv[1], sv[2], sv[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
   int cur = 0;
   for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1) {
     fetch(m + nwarps, bufs + (cur ^ 1) * p.row_chunks);
@@ -318,12 +362,11 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
         const int leaf = lane + 32 * r;
         float s = 0.0f;
         if (leaf < p.leaves && leaf * p.leaf_len < p.K) {
-          // eight running sums (element 8c + e goes to sum e) as four f32x2 pairs; each square is rounded
-          // before it is added, as x * x followed by a sum does
+          // eight running sums (element 8c + e goes to sum e) as four f32x2 pairs
           f32x2 acc[4];
           const int nchunk = min(p.leaf_len / 8, int((p.K - int64_t(leaf) * p.leaf_len) / 8));
           {
-            const uint4 v = row_s[(leaf << 4) | (leaf & 15)];
+            const uint4 v = row_s[swz(leaf << 4)];
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -332,7 +375,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
             }
           }
           for (int c = 1; c < nchunk; ++c) {
-            const uint4 v = row_s[(leaf << 4) | (c ^ (leaf & 15))];
+            const uint4 v = row_s[swz((leaf << 4) | c)];
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -360,22 +403,34 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
 
     const int64_t b = m / p.S;
     const bool use_noisy = p.mask == nullptr || __ldg(p.mask + (m % p.S)) != 0;
+    const int t = int(b % p.batches) * p.variants + (use_noisy ? 0 : 1);  // batches == 1: one shared row
+    const uint4 *m1_row = m1_s + t * kc;
+    const uint4 *sh_row_s = sh_s + t * kc;
     const __nv_bfloat16 *mod_row = (use_noisy ? p.noisy : p.clean) + b * p.mod_stride;
     const __nv_bfloat16 *sh_base = use_noisy ? p.shift : p.shift_clean;
-    const __nv_bfloat16 *sh_row = sh_base ? sh_base + b * p.mod_stride : nullptr;
+    const __nv_bfloat16 *sh_row = kShift ? sh_base + b * p.mod_stride : nullptr;
     uint8_t *q_row = p.q + m * (p.K >> 1);
-
     // scale-byte offset = row part + group part (fibo/fp4.py:60)
     const int64_t sf_row = (m >> 7) * (p.K / 64 * 512) + (m & 31) * 16 + ((m & 127) >> 5) * 4;
+
     auto group = [&](int g) {
       uint32_t xu[8], wu[8], mv[8], sv[8];
       unpack16(row_s[swz(2 * g)], row_s[swz(2 * g + 1)], xu);
-      unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), wu);
-      load_mod8(mod_row, int64_t(g) * 16, p.mods_vec, mv);
-      load_mod8(mod_row, int64_t(g) * 16 + 8, p.mods_vec, mv + 4);
-      if (sh_row) {
-        load_mod8(sh_row, int64_t(g) * 16, p.mods_vec, sv);
-        load_mod8(sh_row, int64_t(g) * 16 + 8, p.mods_vec, sv + 4);
+      if (kTables) {
+        unpack16(w_s[g], w_s[half + g], wu);
+        unpack16(m1_row[g], m1_row[half + g], mv);
+        if (kShift) unpack16(sh_row_s[g], sh_row_s[half + g], sv);
+      } else {
+        uint32_t md[8];
+        unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), wu);
+        load_mod8(mod_row, int64_t(g) * 16, p.mods_vec, md);
+        load_mod8(mod_row, int64_t(g) * 16 + 8, p.mods_vec, md + 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mv[i] = badd2(kOne2, md[i]);
+        if (kShift) {
+          load_mod8(sh_row, int64_t(g) * 16, p.mods_vec, sv);
+          load_mod8(sh_row, int64_t(g) * 16 + 8, p.mods_vec, sv + 4);
+        }
       }
       uint32_t y[8];
 #pragma unroll
@@ -383,8 +438,8 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
         // bf16(bf16(bf16(x * rstd) * w) * bf16(1 + mod)) [+ shift, rounded]
         uint32_t v = f2_bf2(mul2(bf2_f2(xu[i]), rstd2));
         v = bmul2(v, wu[i]);
-        v = bmul2(v, badd2(kOne2, mv[i]));
-        if (sh_row) v = badd2(v, sv[i]);
+        v = bmul2(v, mv[i]);
+        if (kShift) v = badd2(v, sv[i]);
         y[i] = v;
       }
       uint32_t sb;
@@ -401,6 +456,37 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     __syncwarp();  // every lane is done with this buffer before it is refilled
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+template <int kWarps, bool kTables, bool kShift>
+int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
+  auto kernel = norm_scale_fp4_kernel<kWarps, kTables, kShift>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_status(e, "qe_norm_scale_fp4: smem attribute");
+    attr_set[dev] = true;
+  }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kWarps * 32, smem) != cudaSuccess || occ < 1)
+    occ = 1;
+  const int64_t blocks_needed = (p.padded + kWarps - 1) / kWarps;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(blocks_needed, int64_t(sm_count()) * occ));
+  kernel<<<dim3(unsigned(blocks)), dim3(kWarps * 32), smem, stream>>>(p);
+  return cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
+}
+
+template <bool kTables, bool kShift>
+int launch_norm_warps(int warps, const NormParams &p, size_t smem, cudaStream_t stream) {
+  switch (warps) {
+    case 16: return launch_norm_typed<16, kTables, kShift>(p, smem, stream);
+    case 8: return launch_norm_typed<8, kTables, kShift>(p, smem, stream);
+    case 6: return launch_norm_typed<6, kTables, kShift>(p, smem, stream);
+    case 4: return launch_norm_typed<4, kTables, kShift>(p, smem, stream);
+    default: return launch_norm_typed<2, kTables, kShift>(p, smem, stream);
+  }
 }
 
 // ---- SiLU(gate) * value -> NVFP4 ---------------------------------------------------------------
@@ -555,31 +641,34 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   for (const void *ptr : {noisy, clean, shift, shift_clean})
     if (ptr && !qe::aligned16(ptr)) vec = false;
   p.mods_vec = vec ? 1 : 0;
-  // shared memory: two row buffers per warp, each in whole 256-byte leaves (the swizzle stays inside a leaf)
+  // shared memory: two row buffers per warp (whole 256-byte leaves) plus, when they fit, the per-column
+  // constant tables; pick the warps per CTA that keep the most warps resident per SM
   p.row_chunks = int32_t((K + 127) / 128 * 16);
-  const size_t per_warp = 2 * size_t(p.row_chunks) * 16;
+  p.batches = int32_t(mod_stride == 0 ? 1 : (M / S));
+  p.variants = mask ? 2 : 1;
+  const bool has_shift = shift != nullptr;
+  const size_t row_pair = 2 * size_t(p.row_chunks) * 16;
   constexpr size_t kSmemMax = 227 * 1024;
-  const int warps = per_warp * 8 <= kSmemMax ? 8 : per_warp * 4 <= kSmemMax ? 4 : 2;
-  const size_t smem = per_warp * size_t(warps);
-  if (smem > kSmemMax) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for two rows per warp");
-  // the shared-memory opt-in is per device context: remember it per device
-  static bool attr_set[64][3] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  auto kernel = warps == 8 ? qe::norm_scale_fp4_kernel<8>
-                           : warps == 4 ? qe::norm_scale_fp4_kernel<4> : qe::norm_scale_fp4_kernel<2>;
-  const int variant = warps == 8 ? 2 : warps == 4 ? 1 : 0;
-  if (!attr_set[dev][variant]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemMax));
-    if (e != cudaSuccess) return qe::cuda_status(e, "qe_norm_scale_fp4: smem attribute");
-    attr_set[dev][variant] = true;
+  const size_t tables = qe::norm_table_bytes(K, int64_t(p.batches) * p.variants, has_shift);
+  const bool use_tables = tables <= 64 * 1024;
+  int best_warps = 0, best_resident = 0;
+  size_t best_smem = 0;
+  for (int w : {16, 8, 6, 4, 2}) {
+    const size_t smem = size_t(w) * row_pair + (use_tables ? tables : 0);
+    if (smem > kSmemMax) continue;
+    const int per_sm = std::min<int>(int(kSmemMax / smem), 32 / w);
+    if (per_sm * w > best_resident) {
+      best_resident = per_sm * w;
+      best_warps = w;
+      best_smem = smem;
+    }
   }
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, warps * 32, smem) != cudaSuccess || occ < 1) occ = 1;
-  const int64_t blocks_needed = (padded + warps - 1) / warps;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(blocks_needed, int64_t(qe::sm_count()) * occ));
-  kernel<<<dim3(unsigned(blocks)), dim3(warps * 32), smem, static_cast<cudaStream_t>(stream)>>>(p);
-  int s = qe::cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
+  if (best_warps == 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for two rows per warp");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int s = use_tables ? (has_shift ? qe::launch_norm_warps<true, true>(best_warps, p, best_smem, st)
+                                  : qe::launch_norm_warps<true, false>(best_warps, p, best_smem, st))
+                     : (has_shift ? qe::launch_norm_warps<false, true>(best_warps, p, best_smem, st)
+                                  : qe::launch_norm_warps<false, false>(best_warps, p, best_smem, st));
   return s ? s : qe::ok();
 }
 
