@@ -81,9 +81,24 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
-// bf16x2 word -> exact f32x2
+// bf16x2 word -> exact f32x2, on the FMA pipe: x * 1 + (-0) with bf16 multiplicands is x exactly (the -0
+// addend keeps the sign of a zero)
 __device__ __forceinline__ f32x2 bf2_f2(uint32_t u) {
-  return pk2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  float lo, hi;
+  asm("{\n .reg .b16 l, h, one;\n mov.b32 {l, h}, %2;\n mov.b16 one, 0x3f80;\n"
+      " fma.rn.f32.bf16 %0, l, one, %3;\n fma.rn.f32.bf16 %1, h, one, %3;\n}\n"
+      : "=f"(lo), "=f"(hi)
+      : "r"(u), "f"(-0.0f));
+  return pk2(lo, hi);
+}
+
+// a0 += lo(u)^2, a1 += hi(u)^2 with one rounding each: the square of a bf16 value is exact in fp32, so this
+// equals rounding x * x and then adding it
+__device__ __forceinline__ void sq_acc2(uint32_t u, float &a0, float &a1) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
+      " fma.rn.f32.bf16 %0, l, l, %0;\n fma.rn.f32.bf16 %1, h, h, %1;\n}\n"
+      : "+f"(a0), "+f"(a1)
+      : "r"(u));
 }
 // f32x2 -> bf16x2 word, each half rounded to nearest even
 __device__ __forceinline__ uint32_t f2_bf2(f32x2 v) {
@@ -362,29 +377,19 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
         const int leaf = lane + 32 * r;
         float s = 0.0f;
         if (leaf < p.leaves && leaf * p.leaf_len < p.K) {
-          // eight running sums (element 8c + e goes to sum e) as four f32x2 pairs
-          f32x2 acc[4];
+          // eight running sums (element 8c + e goes to sum e); the first chunk seeds them (0 + x*x = x*x)
+          float r[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
           const int nchunk = min(p.leaf_len / 8, int((p.K - int64_t(leaf) * p.leaf_len) / 8));
-          {
-            const uint4 v = row_s[swz(leaf << 4)];
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const f32x2 f = bf2_f2(u[i]);
-              acc[i] = mul2(f, f);
-            }
-          }
-          for (int c = 1; c < nchunk; ++c) {
+          for (int c = 0; c < nchunk; ++c) {
             const uint4 v = row_s[swz((leaf << 4) | c)];
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const f32x2 f = bf2_f2(u[i]);
-              acc[i] = fma2(f, f, acc[i]);  // f * f is exact for bf16 f: same as rounding, then adding
-            }
+            sq_acc2(v.x, r[0], r[1]);
+            sq_acc2(v.y, r[2], r[3]);
+            sq_acc2(v.z, r[4], r[5]);
+            sq_acc2(v.w, r[6], r[7]);
           }
           // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7))
-          const float2 a0 = up2(acc[0]), a1 = up2(acc[1]), a2 = up2(acc[2]), a3 = up2(acc[3]);
+          const float2 a0 = make_float2(r[0], r[1]), a1 = make_float2(r[2], r[3]);
+          const float2 a2 = make_float2(r[4], r[5]), a3 = make_float2(r[6], r[7]);
           const float2 t = up2(add2(pk2(a0.x, a2.x), pk2(a0.y, a2.y)));
           const float2 u2 = up2(add2(pk2(a1.x, a3.x), pk2(a1.y, a3.y)));
           const float2 v2 = up2(add2(pk2(t.x, t.y), pk2(u2.x, u2.y)));
