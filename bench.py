@@ -291,11 +291,26 @@ def run_ours(args, rank, world, local):
     if pool.device_errors():
         raise RuntimeError("a kernel reported an out-of-range slot")
 
-    # ---- e2e: the same turns through the public API, result probe read back every turn ------------
-    probe = torch.empty(2, dtype=torch.int64, pin_memory=True)
-    h2d0 = pool.h2d_bytes
-    for _ in range(args.warmup):
+    # ---- e2e: the same turns through the public API; every turn's result probe (the pool's device error flag
+    # and 8 bytes of the last gathered row) is copied to pinned host memory and read back, one turn behind so the
+    # host bookkeeping of turn t+1 overlaps the device work of turn t, as a serving loop would run it
+    probes = [torch.empty(2, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+
+    def issue_probe(k):
+        probe_dev = torch.stack([pool._err.to(torch.int64)[0], sess.out[-1, 1, -1, -1, -4:].view(torch.int64)[0]])
+        probes[k % 2].copy_(probe_dev, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return ev
+
+    def read_probe(k, ev):
+        ev.synchronize()
+        if int(probes[k % 2][0]) != 0:
+            raise RuntimeError("device error flag set")
+
+    for k in range(args.warmup):
         sess.api_turn()
+        read_probe(k, issue_probe(k))
     torch.cuda.synchronize()
     h2d0 = pool.h2d_bytes
     barrier(world)
@@ -303,24 +318,24 @@ def run_ours(args, rank, world, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     wall0 = time.perf_counter()
-    for _ in range(args.steps):
+    pending = None
+    for k in range(args.steps):
         sess.api_turn()
-        # result probe: the pool's device error flag and 8 bytes of the last gathered row
-        probe_dev = torch.stack([pool._err.to(torch.int64)[0], sess.out[-1, 1, -1, -1, -4:].view(torch.int64)[0]])
-        probe.copy_(probe_dev, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        if int(probe[0]) != 0:
-            raise RuntimeError("device error flag set")
+        ev = issue_probe(k)
+        if pending is not None:
+            read_probe(*pending)
+        pending = (k, ev)
+    read_probe(*pending)
     e1.record(stream)
     torch.cuda.synchronize()
     wall_ms = (time.perf_counter() - wall0) * 1e3
     barrier(world)
     e2e_ms = max_over_ranks(max(e0.elapsed_time(e1), wall_ms), world, device)
     h2d_per_step = (pool.h2d_bytes - h2d0) / args.steps
-    d2h_per_step = probe.numel() * probe.element_size()
+    d2h_per_step = probes[0].numel() * probes[0].element_size()
 
     result = {}
-    if not args.no_extras:
+    if not args.no_extras and world == 1:  # side measurements are per-GPU; the scaling runs skip them
         result = extras(pool, sess, device)
     return dict(elapsed_ms=elapsed_ms, avg_gather_ms=avg_gather_ms, clocks=clock_info, e2e_ms=e2e_ms,
                 h2d=h2d_per_step, d2h=d2h_per_step, extras=result)

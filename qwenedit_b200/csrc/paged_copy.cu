@@ -8,7 +8,7 @@
 // A pool is a stack of planes (layer x {K,V}), each [rows, row_bytes]; a token's K or V for one layer is
 // one row of H*D elements (6 KB for the Qwen-Image DiT, 1 KB for the text encoder). Every row copy is
 // a 16-byte-vectorised, fully coalesced warp copy: lane i moves bytes [16 i, 16 i + 16) of each 512-byte
-// stripe, with up to kUnroll loads in flight per lane before the matching stores. Each warp walks its
+// stripe, with 8 or 16 loads in flight per lane before the matching stores. Each warp walks its
 // rows through the slot list (token-granular, page_size 1) or the block table (page_size P). The grid is
 // persistent: a multiple of the SM count, warps striding over the (plane, token) rows.
 #include <algorithm>
@@ -34,7 +34,6 @@ int sm_count() {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 8;
 
 struct Planes {
   char *base;
@@ -78,7 +77,9 @@ __device__ __forceinline__ void store_v<int4>(int4 *p, int4 v) {
   st_stream(p, v);
 }
 
-template <typename V, int kMode, bool kGather, bool kPtrs>
+// kUnroll vectors per lane are loaded before any is stored: 16 for rows of 6 KiB and more (a whole DiT row in
+// flight per warp), 8 for smaller rows.
+template <typename V, int kMode, bool kGather, bool kPtrs, int kUnroll>
 __global__ void __launch_bounds__(kThreads) paged_copy_kernel(CopyParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
@@ -371,23 +372,30 @@ int launch_bulk(const CopyParams &p, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "paged bulk copy launch");
 }
 
-template <typename V, int kMode, bool kGather, bool kPtrs>
-int launch_typed(const CopyParams &p, cudaStream_t stream) {
+template <typename V, int kMode, bool kGather, bool kPtrs, int kUnroll>
+int launch_unrolled(const CopyParams &p, cudaStream_t stream) {
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
     int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, paged_copy_kernel<V, kMode, kGather, kPtrs>, kThreads, 0) !=
-            cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, paged_copy_kernel<V, kMode, kGather, kPtrs, kUnroll>,
+                                                      kThreads, 0) != cudaSuccess ||
         b <= 0)
-      b = 4;
+      b = 2;
     blocks_per_sm = b;
   }
   const int64_t rows = int64_t(p.n_planes) * p.n_tokens;
   const int64_t warps_per_block = kThreads / 32;
   int64_t blocks = std::min<int64_t>((rows + warps_per_block - 1) / warps_per_block, int64_t(sm_count()) * blocks_per_sm);
   blocks = std::max<int64_t>(blocks, 1);
-  paged_copy_kernel<V, kMode, kGather, kPtrs><<<dim3(unsigned(blocks)), dim3(kThreads), 0, stream>>>(p);
+  paged_copy_kernel<V, kMode, kGather, kPtrs, kUnroll><<<dim3(unsigned(blocks)), dim3(kThreads), 0, stream>>>(p);
   return cuda_status(cudaGetLastError(), "paged copy launch");
+}
+
+template <typename V, int kMode, bool kGather, bool kPtrs>
+int launch_typed(const CopyParams &p, cudaStream_t stream) {
+  const int64_t vpr = p.row_bytes / int64_t(sizeof(V));
+  if (vpr >= 32 * 12) return launch_unrolled<V, kMode, kGather, kPtrs, 16>(p, stream);
+  return launch_unrolled<V, kMode, kGather, kPtrs, 8>(p, stream);
 }
 
 bool planes_aligned(const qe_planes &pl, int a) {
