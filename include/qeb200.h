@@ -179,6 +179,18 @@ int qe_index_shuffle_free(qe_index *ix, uint64_t seed);
  * tokens, out[3] = live tree nodes (excluding the root). */
 int qe_index_usage(qe_index *ix, int64_t out[4]);
 
+/* ---- prefix keys (host) -------------------------------------------------------------------------
+ * Chained 63-bit ids of multi_turn/cache/keys.py, computed natively (the reference loops over text tokens in
+ * Python, keys.py:81-84, :94-96, :100-102). BLAKE2b-128 of length-prefixed parts, RFC 7693. */
+
+/* BLAKE2b with a 16-byte digest of msg[0..len) (hashlib.blake2b(digest_size=16)). */
+int qe_blake2b16(const uint8_t *msg, int64_t len, uint8_t *out16);
+/* out[i] = id of text token i chained from `prev` (keys.py:57-58 applied along tokens[0..n)). */
+int qe_keys_text_chain(int64_t prev, const int64_t *tokens, int64_t n, int64_t *out);
+/* out[i] = id of token i of an n-token image block after `prev` with content key content[0..len)
+ * (keys.py:42-54). */
+int qe_keys_block_ids(int64_t prev, const uint8_t *content, int64_t len, int64_t n, int64_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,9 @@ SIGNATURES: dict[str, list] = {
     "qe_index_usage": [c_void_p, _P64],
     "qe_index_shuffle_free": [c_void_p, c_uint64],
     "qe_set_paged_copy_mode": [c_int32],
+    "qe_blake2b16": [c_void_p, c_int64, c_void_p],
+    "qe_keys_text_chain": [c_int64, c_void_p, c_int64, c_void_p],
+    "qe_keys_block_ids": [c_int64, c_void_p, c_int64, c_int64, c_void_p],
 }
 
 _lock = threading.Lock()

@@ -8,7 +8,9 @@ identical to the reference so both implementations address the same cached prefi
 * the i-th token of an image block is splitmix64(base + i * 0x9E3779B97F4A7C15) masked to 63 bits, with
   base = id of digest(previous id, b"B", image content key [+ latent h, w for the DiT]).
 
-The whole image block is one vectorised numpy expression; text runs are a short chain of digests.
+Text chains and image blocks are computed by libqeb200 (native BLAKE2b, RFC 7693), one call per run; the
+reference walks text tokens in a Python loop (keys.py:81-84). Root / content keys stay on hashlib (one digest
+each).
 """
 
 from __future__ import annotations
@@ -18,11 +20,10 @@ from collections.abc import Sequence
 
 import numpy as np
 
+from qwenedit_b200 import _lib
+
 DIGEST = 16
 MASK63 = (1 << 63) - 1
-_GOLDEN = np.uint64(0x9E3779B97F4A7C15)
-_MIX1 = np.uint64(0xBF58476D1CE4E5B9)
-_MIX2 = np.uint64(0x94D049BB133111EB)
 
 
 def _digest(*parts: bytes) -> bytes:
@@ -51,32 +52,36 @@ def _id(digest: bytes) -> int:
     return int.from_bytes(digest[:8], "little") & MASK63
 
 
-def _mix63(x: np.ndarray) -> np.ndarray:
-    """splitmix64's output function (Steele, Lea & Flood 2014), truncated to 63 bits."""
-    with np.errstate(over="ignore"):
-        x = (x ^ (x >> np.uint64(30))) * _MIX1
-        x = (x ^ (x >> np.uint64(27))) * _MIX2
-        x = x ^ (x >> np.uint64(31))
-    return (x & np.uint64(MASK63)).astype(np.int64)
+def _i64(values) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
 
 
 def block_ids(prev: int, content: bytes, n: int) -> np.ndarray:
     """Ids of an n-token image block that follows id `prev`."""
-    base = np.uint64(_id(_digest(prev.to_bytes(8, "little"), b"B", content)))
-    with np.errstate(over="ignore"):
-        return _mix63(base + np.arange(n, dtype=np.uint64) * _GOLDEN)
+    out = np.empty(n, np.int64)
+    buf = np.frombuffer(content, dtype=np.uint8) if content else np.zeros(1, np.uint8)
+    _lib.call("qe_keys_block_ids", int(prev), buf.ctypes.data, len(content), n, out.ctypes.data)
+    return out
+
+
+def text_chain(prev: int, tokens) -> np.ndarray:
+    """Ids of text tokens chained from id `prev` (one native call for the whole run)."""
+    toks = _i64(tokens)
+    out = np.empty(len(toks), np.int64)
+    if len(toks):
+        _lib.call("qe_keys_text_chain", int(prev), toks.ctypes.data, len(toks), out.ctypes.data)
+    return out
 
 
 def text_id(prev: int, token: int) -> int:
     """Id of a text token that follows id `prev`."""
-    return _id(_digest(prev.to_bytes(8, "little"), b"t", int(token).to_bytes(8, "little", signed=True)))
+    return int(text_chain(prev, [token])[0])
 
 
 def _text_chain(prev: int, tokens, out: np.ndarray) -> int:
-    for i, tok in enumerate(tokens):
-        prev = text_id(prev, tok)
-        out[i] = prev
-    return prev
+    ids = text_chain(prev, list(tokens))
+    out[:] = ids
+    return int(ids[-1]) if len(ids) else prev
 
 
 def virtual_ids(root: bytes, segments: Sequence[tuple[int, int, bool]], text_indices: Sequence[int],

@@ -81,3 +81,37 @@ def test_layout_errors_raise():
         keys.virtual_ids(b"r", ((0, 5, True),), [], [], [b"x"], [(2, 2)])
     with pytest.raises(ValueError):
         keys.virtual_ids(b"r", ((0, 2, False),), [0, 1], [5, 6], [b"x"], [])
+
+
+def test_native_blake2b_matches_hashlib():
+    import ctypes
+    import hashlib
+
+    from qwenedit_b200 import _lib
+
+    rng = np.random.default_rng(0)
+    for n in (0, 1, 41, 127, 128, 129, 255, 256, 257, 1000, 4096):
+        msg = rng.integers(0, 256, size=n, dtype=np.uint8).tobytes()
+        out = (ctypes.c_uint8 * 16)()
+        buf = np.frombuffer(msg, np.uint8) if n else np.zeros(1, np.uint8)
+        _lib.call("qe_blake2b16", buf.ctypes.data, n, ctypes.addressof(out))
+        assert bytes(out) == hashlib.blake2b(msg, digest_size=16).digest(), n
+
+
+def test_native_text_chain_matches_the_digest_definition():
+    import hashlib
+
+    def ref_text_id(prev, token):  # keys.py:57-58 written out with hashlib
+        h = hashlib.blake2b(digest_size=16)
+        for part in (prev.to_bytes(8, "little"), b"t", int(token).to_bytes(8, "little", signed=True)):
+            h.update(len(part).to_bytes(8, "little"))
+            h.update(part)
+        return int.from_bytes(h.digest()[:8], "little") & ((1 << 63) - 1)
+
+    prev = 12345
+    toks = [0, 1, -5, 2**40, 151643, 7]
+    want = []
+    for t in toks:
+        prev = ref_text_id(prev, t)
+        want.append(prev)
+    np.testing.assert_array_equal(keys.text_chain(12345, toks), np.array(want, np.int64))
