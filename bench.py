@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
+    ap.add_argument("--workload", choices=["edit_1k", "serving"], default="edit_1k",
+                    help="edit_1k: the 1K-edit turn (default, the headline); serving: 64 mixed 1K/2K sessions")
     ap.add_argument("--profile", choices=["gather", "append", "norm", "silu"], default=None,
                     help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
     return ap.parse_args()
@@ -474,6 +476,145 @@ def cpu_turns(steps: int, warmup: int, layers: int = CPU_SAMPLE_LAYERS):
     return sample_bytes / per_turn / 1e9, per_turn, threads
 
 
+# ---- serving mix: 64 sessions, half 1K and half 2K, hashed to GPUs -------------------------------------
+SERVING_SESSIONS = 64
+SERVING_ACTIVE = 2  # sessions active at once per GPU: a 2K prefix is 12.5 GB of a 24 GiB pool
+IMAGE_TOKENS = {"1k": 4096, "2k": 16384}
+
+
+def serving_plan(seed: int = 0):
+    """Session specs shared by every rank: size, turns (Zipf(1.2) capped at 10), box-edit fraction per turn."""
+    rng = np.random.default_rng(seed)
+    plan = []
+    for i in range(SERVING_SESSIONS):
+        turns = int(min(10, rng.zipf(1.2)))
+        boxes = [float(rng.uniform(0.1, 0.4)) if rng.random() < 0.2 else 1.0 for _ in range(turns)]
+        plan.append({"id": f"session-{i:02d}", "size": "1k" if i % 2 == 0 else "2k", "boxes": boxes})
+    return plan
+
+
+def run_serving(args, rank, world, local):
+    """Each rank serves the sessions it owns (stable hash) from its own 24 GiB pool. A turn: match the prefix
+    (text + current image); on a full hit, gather it once per denoising step; on a miss (evicted) store the
+    recomputed prefix; then append the turn's new image tokens. A box edit recomputes the last `frac` of the
+    image tokens (the radix cache can reuse only a prefix), so only those are appended."""
+    from qwenedit_b200.paged import PagedKVPool
+    from qwenedit_b200.sessions import SessionRouter
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    router = SessionRouter(rank, world)
+    plan = [p for p in serving_plan() if router.owns(p["id"])]
+    pool = PagedKVPool("dit", L, H, D, POOL_GIB << 30, torch.bfloat16, device, page_size=PAGE)
+    pool.index.shuffle_free(2000 + rank)
+    stream = torch.cuda.current_stream(device)
+    rng = np.random.default_rng(100 + rank)
+    new_kv = torch.empty(L, 2, IMAGE_TOKENS["2k"] + TEXT, H, D, dtype=torch.bfloat16, device=device)
+    new_kv.normal_()
+    outs = {k: torch.empty(L, 2, TEXT + n, H, D, dtype=torch.bfloat16, device=device) for k, n in IMAGE_TOKENS.items()}
+    state = {}
+    for sp in plan:
+        n_img = IMAGE_TOKENS[sp["size"]]
+        state[sp["id"]] = {"text": rng.integers(1, 1 << 62, size=TEXT), "image": rng.integers(1, 1 << 62, size=n_img),
+                           "turn": 0}
+    # SERVING_ACTIVE sessions are active at a time per GPU (the rest queue in a seeded order); requests of the
+    # active sessions interleave round-robin, and a finished session hands its slot to the next in the queue
+    queue = [plan[i] for i in rng.permutation(len(plan))]
+    active, order = [], []
+    while queue or active:
+        while queue and len(active) < SERVING_ACTIVE:
+            active.append(queue.pop(0))
+        for sp in list(active):
+            t = state[sp["id"]]["turn"]
+            order.append((sp, t))
+            state[sp["id"]]["turn"] += 1
+            if t + 1 >= len(sp["boxes"]):
+                active.remove(sp)
+    step_events, moved, hits, misses = [], 0, 0, 0
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for sp, t in order:
+        st = state[sp["id"]]
+        vids = np.concatenate([st["text"], st["image"]])
+        total = len(vids)
+        m = pool.match(vids)
+        if m.length == total:
+            hits += 1
+            out = outs[sp["size"]]
+            for _ in range(STEPS_PER_TURN):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                pool.gather_into(m.indices, out)
+                b.record(stream)
+                step_events.append((a, b))
+                moved += 2 * L * 2 * total * ROW
+        else:  # evicted (or first turn): the DiT recomputes the uncached tail; store it
+            misses += 1
+            slots = pool.alloc(total - m.length)
+            if slots is not None:
+                pool.write(slots, new_kv[:, :, : total - m.length])
+                idx = np.concatenate([m.indices._qe_host, slots._qe_host]) if m.length else slots._qe_host
+                it = torch.from_numpy(idx.copy())
+                it._qe_host = it.numpy()
+                pool.insert(vids, it, owned_from=m.length)
+                moved += 2 * L * 2 * (total - m.length) * ROW
+        m.release()
+        # the turn's output becomes the next conditioning image: a box edit changes the last `frac` of it
+        frac = sp["boxes"][t]
+        n_img = len(st["image"])
+        keep = n_img - int(round(frac * n_img)) // PAGE * PAGE
+        new_ids = rng.integers(1, 1 << 62, size=n_img - keep)
+        st["image"] = np.concatenate([st["image"][:keep], new_ids])
+        nv = np.concatenate([st["text"], st["image"]])
+        m2 = pool.match(nv)
+        slots = pool.alloc(len(nv) - m2.length)
+        if slots is not None:
+            pool.write(slots, new_kv[:, :, : len(nv) - m2.length])
+            idx = np.concatenate([m2.indices._qe_host, slots._qe_host]) if m2.length else slots._qe_host
+            it = torch.from_numpy(idx.copy())
+            it._qe_host = it.numpy()
+            pool.insert(nv, it, owned_from=m2.length)
+            moved += 2 * L * 2 * (len(nv) - m2.length) * ROW
+        m2.release()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    elapsed = max_over_ranks(t0.elapsed_time(t1), world, device)
+    steps = [a.elapsed_time(b) for a, b in step_events]
+    if pool.device_errors():
+        raise RuntimeError("a paged copy kernel reported an error")
+    total_moved = torch.tensor([float(moved), float(hits), float(misses), float(len(order)),
+                                float(pool.usage()["evicted_tokens"])], dtype=torch.float64, device=device)
+    all_steps = [steps]
+    if world > 1:
+        torch.distributed.all_reduce(total_moved)
+        gathered = [None] * world
+        torch.distributed.all_gather_object(gathered, steps)
+        all_steps = gathered
+    flat = sorted(x for s_ in all_steps for x in s_)
+    pct = (lambda q: flat[min(len(flat) - 1, int(q * len(flat)))]) if flat else (lambda q: None)
+    moved_all, hits_all, misses_all, turns_all, evicted_all = [float(v) for v in total_moved.tolist()]
+    if rank == 0:
+        peak, _ = measured_peak()
+        value = moved_all / elapsed / 1e6
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": int(turns_all),
+            "warmup": 0, "ms_per_step": round(elapsed / max(turns_all, 1) * world, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen_image_2.1_serving_64_sessions", "sessions": SERVING_SESSIONS,
+                       "sizes": "half 1K (4096+512 prefix), half 2K (16384+512 prefix)",
+                       "turns": "Zipf(1.2) capped at 10", "box_edits": "20% of turns, last 10-40% of image tokens",
+                       "pool_gib_per_gpu": POOL_GIB, "page_tokens": PAGE, "partition": "stable hash of session id",
+                       "active_sessions_per_gpu": SERVING_ACTIVE},
+            "frac_of_measured_hbm_per_gpu": round(value / world / peak, 4),
+            "step_ms_p50": round(pct(0.5), 4) if flat else None, "step_ms_p99": round(pct(0.99), 4) if flat else None,
+            "turns": int(turns_all), "prefix_hits": int(hits_all), "prefix_misses": int(misses_all),
+            "evicted_tokens": int(evicted_all), "gpu_launches": len(flat) + 2 * int(turns_all),
+        }), flush=True)
+
+
 def profile_case(kind: str) -> None:
     """A small case of one kernel for ncu captures: inputs > L2, a few GB on the device, 6 launches."""
     from types import SimpleNamespace
@@ -541,6 +682,11 @@ def main():
         }), flush=True)
         return
 
+    if args.workload == "serving":
+        run_serving(args, rank, world, local)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     r = run_ours(args, rank, world, local)
     peak, peak_src = measured_peak()
     value = TURN_BYTES * world / (r["elapsed_ms"] / args.steps) / 1e6  # GB/s over all ranks
