@@ -412,7 +412,7 @@ def _time_kernel(fn, flush, iters=10):
 def nvfp4_extras(device, peak):
     from types import SimpleNamespace
 
-    from qwenedit_b200.fp4 import norm_scale_fp4, silu_mul_fp4
+    from qwenedit_b200.fp4 import norm_scale_amax, norm_scale_fp4, silu_mul_amax, silu_mul_fp4
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2, rewritten between launches
     out = {}
@@ -428,6 +428,11 @@ def nvfp4_extras(device, peak):
         nbytes = T * K * 2 + K * 2 * 3 + T * K // 2 + pad * K // 16
         out[f"norm_scale_fp4_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
                                        "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
+        if T == 32768:  # the calibration pre-pass reads x alone
+            ms = _time_kernel(lambda: norm_scale_amax(x, norm, scale, None, None, shift=shift), flush)
+            nbytes = T * K * 2 + K * 2 * 3
+            out[f"norm_scale_amax_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+                                            "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
     K = 12288
     for T in (4096, 16384):
         g = torch.randn(T, K, dtype=torch.bfloat16, device=device)
@@ -438,6 +443,11 @@ def nvfp4_extras(device, peak):
         nbytes = 2 * T * K * 2 + T * K // 2 + pad * K // 16
         out[f"silu_mul_fp4_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
                                      "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
+        if T == 16384:
+            ms = _time_kernel(lambda: silu_mul_amax(g, v), flush)
+            nbytes = 2 * T * K * 2
+            out[f"silu_mul_amax_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+                                          "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
     return out
 
 

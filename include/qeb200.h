@@ -140,6 +140,18 @@ int qe_silu_table_init(uint16_t *table, void *stream);
 int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
                     uint8_t *sf, const uint16_t *silu_table, void *stream);
 
+/* Calibration pre-passes: *amax = max |y| over all M*K values of the y the matching quantiser would encode
+ * (the bf16 result of the norm/adaLN or SiLU*mul arithmetic, as fp32). Replaces the bf16 pass the reference
+ * runs on a layer's first call to set its activation scale, `x2.float().abs().amax()` in
+ * pipeline/fp4.py:33-35 (fused caller: fibo/fp4.py:128-134); gs = 448*6 / (max(amax, 1e-8) * headroom).
+ * amax is one device fp32, cleared on `stream` by the call; M = 0 leaves it 0. No codes or scales are
+ * written. Arguments otherwise as the quantisers above. */
+int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
+                       const void *shift, const void *shift_clean, int64_t M, int64_t S, int64_t K,
+                       int64_t mod_stride, float eps, float *amax, void *stream);
+int qe_silu_mul_amax(const void *gate, const void *value, int64_t M, int64_t K, const uint16_t *silu_table,
+                     float *amax, void *stream);
+
 /* ---- prefix index: radix tree + slot allocator + LRU eviction (host) -------------------------
  *
  * Restates the behaviour of SGLang's RadixCache (page_size 1 and paged) and TokenToKVPoolAllocator

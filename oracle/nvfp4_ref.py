@@ -147,9 +147,10 @@ def bf16_values_norm_scale(x, weight, eps, noisy, clean=None, noise_mask=None, s
 
 
 def global_scale(y: torch.Tensor, headroom: float = 4.0) -> float:
-    """448 * 6 / (amax * headroom) in float32 (tests/test_fibo_fp4.py:18-19; pipeline/fp4.py:33-35)."""
+    """448 * 6 / (amax * headroom) in float32, as the reference writes it (tests/test_fibo_fp4.py:18-19;
+    pipeline/fp4.py:33-35): a Python scalar over a tensor, which torch evaluates as reciprocal then multiply."""
     amax = y.float().abs().amax().clamp(min=1e-8) * headroom
-    return float((torch.tensor(448.0 * 6.0) / amax).to(torch.float32))
+    return float((448.0 * 6.0 / amax).to(torch.float32))
 
 
 __all__ = ["build", "lib", "norm_scale_fp4_ref", "silu_mul_fp4_ref", "bf16_values_norm_scale", "global_scale"]

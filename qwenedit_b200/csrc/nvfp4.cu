@@ -255,6 +255,7 @@ struct NormParams {
   int32_t batches;     // modulation rows staged per variant
   int32_t variants;    // 1, or 2 with a token mask (noisy, clean)
   float eps;
+  float *amax;         // amax mode: max |y| over the whole tensor (the calibration pre-pass)
 };
 
 // Shared-memory chunk of 16-byte chunk c of a row: leaf-major with an XOR swizzle inside the leaf, chosen so
@@ -304,7 +305,8 @@ inline size_t norm_table_bytes(int64_t K, int64_t rows, bool shift) {
 // the per-column constants (w, the pre-rounded bf16(1 + scale) rows of every batch and mask variant, the
 // shift rows) in shared memory, so the per-row work reads them from there; without, they come from global
 // memory. In the element-wise pass lane l owns the 16-value groups g = l + 32 i.
-template <int kWarps, bool kTables, bool kShift>
+// kAmax: the calibration pre-pass — the same y, reduced to max |y| instead of quantised and stored.
+template <int kWarps, bool kTables, bool kShift, bool kAmax>
 __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams p) {
   extern __shared__ uint4 smem[];
   const int lane = threadIdx.x & 31;
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + int64_t(wid) * 2 * p.row_chunks;
   const int64_t warp0 = int64_t(blockIdx.x) * kWarps + wid;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
-  const float gs = __ldg(p.gs);
+  const float gs = kAmax ? 1.0f : __ldg(p.gs);
   const float inv_gs = __fdiv_rn(1.0f, gs);
   const float kf = float(p.K);
 
@@ -331,6 +333,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     cp_async_commit();
   };
   fetch(warp0, bufs);
+  uint32_t amax_w = 0u;  // kAmax: running bf16x2 max of |y|
 
   if (kTables) {
     for (int c = threadIdx.x; c < kc; c += kWarps * 32) w_s[gix(c, half)] = __ldg(p.w + c);
@@ -360,7 +363,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     cp_async_wait_1();  // this row's copies (all but the newest group) have landed
     __syncwarp();
     if (m >= p.M) {  // padding rows of the last 128-row tile: zero scales, no codes
-      zero_sf_row(p.sf, m, p.K, lane);
+      if (!kAmax) zero_sf_row(p.sf, m, p.K, lane);
       __syncwarp();
       continue;
     }
@@ -447,10 +450,15 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
         if (kShift) v = badd2(v, sv[i]);
         y[i] = v;
       }
-      uint32_t sb;
-      const uint2 codes = quantize16(y, gs, inv_gs, sb);
-      *reinterpret_cast<uint2 *>(q_row + g * 8) = codes;
-      p.sf[sf_row + (g >> 2) * 512 + (g & 3)] = uint8_t(sb);
+      if constexpr (kAmax) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax_w = bmax2(amax_w, y[i] & kAbs2);
+      } else {
+        uint32_t sb;
+        const uint2 codes = quantize16(y, gs, inv_gs, sb);
+        *reinterpret_cast<uint2 *>(q_row + g * 8) = codes;
+        p.sf[sf_row + (g >> 2) * 512 + (g & 3)] = uint8_t(sb);
+      }
     };
     int g = lane;
     for (; g + 32 < gpr; g += 64) {  // two independent groups per iteration
@@ -461,11 +469,17 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     __syncwarp();  // every lane is done with this buffer before it is refilled
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
+  if constexpr (kAmax) {
+    float v = fmaxf(__uint_as_float(amax_w << 16), __uint_as_float(amax_w & 0xffff0000u));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned int *>(p.amax), __float_as_uint(v));  // v >= 0
+  }
 }
 
-template <int kWarps, bool kTables, bool kShift>
+template <int kWarps, bool kTables, bool kShift, bool kAmax>
 int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
-  auto kernel = norm_scale_fp4_kernel<kWarps, kTables, kShift>;
+  auto kernel = norm_scale_fp4_kernel<kWarps, kTables, kShift, kAmax>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -483,15 +497,23 @@ int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
 }
 
-template <bool kTables, bool kShift>
+template <bool kTables, bool kShift, bool kAmax>
 int launch_norm_warps(int warps, const NormParams &p, size_t smem, cudaStream_t stream) {
   switch (warps) {
-    case 16: return launch_norm_typed<16, kTables, kShift>(p, smem, stream);
-    case 8: return launch_norm_typed<8, kTables, kShift>(p, smem, stream);
-    case 6: return launch_norm_typed<6, kTables, kShift>(p, smem, stream);
-    case 4: return launch_norm_typed<4, kTables, kShift>(p, smem, stream);
-    default: return launch_norm_typed<2, kTables, kShift>(p, smem, stream);
+    case 16: return launch_norm_typed<16, kTables, kShift, kAmax>(p, smem, stream);
+    case 8: return launch_norm_typed<8, kTables, kShift, kAmax>(p, smem, stream);
+    case 6: return launch_norm_typed<6, kTables, kShift, kAmax>(p, smem, stream);
+    case 4: return launch_norm_typed<4, kTables, kShift, kAmax>(p, smem, stream);
+    default: return launch_norm_typed<2, kTables, kShift, kAmax>(p, smem, stream);
   }
+}
+
+template <bool kAmax>
+int launch_norm(bool tables, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
+  return tables ? (shift ? launch_norm_warps<true, true, kAmax>(warps, p, smem, st)
+                         : launch_norm_warps<true, false, kAmax>(warps, p, smem, st))
+                : (shift ? launch_norm_warps<false, true, kAmax>(warps, p, smem, st)
+                         : launch_norm_warps<false, false, kAmax>(warps, p, smem, st));
 }
 
 // ---- SiLU(gate) * value -> NVFP4 ---------------------------------------------------------------
@@ -520,6 +542,7 @@ struct SiluParams {
   const uint4 *table;  // kSiluTable bf16 entries
   uint8_t *q;
   uint8_t *sf;
+  float *amax;  // amax mode: max |y| over the whole tensor (the calibration pre-pass)
   int64_t M, K, padded;
 };
 
@@ -531,7 +554,9 @@ __device__ __forceinline__ uint32_t silu_lookup(const uint16_t *tab, uint32_t w)
 }
 
 // A warp item is 32 consecutive 16-value groups of one row, one group per lane; kSiluItems items per
-// iteration so every lane has 8 16-byte loads in flight before it computes.
+// iteration so every lane has 8 16-byte loads in flight before it computes. kAmax: the calibration pre-pass —
+// the same y, reduced to max |y| instead of quantised and stored.
+template <bool kAmax>
 __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
   extern __shared__ uint4 tab4[];
   for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
@@ -543,8 +568,9 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
   const int64_t items = p.M * segs;
   const int64_t warp = (int64_t(blockIdx.x) * kSiluThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * kSiluThreads) >> 5;
-  const float gs = __ldg(p.gs);
+  const float gs = kAmax ? 1.0f : __ldg(p.gs);
   const float inv_gs = __fdiv_rn(1.0f, gs);
+  uint32_t amax_w = 0u;  // kAmax: running bf16x2 max of |y|
 
   for (int64_t it0 = warp; it0 < items; it0 += nwarps * kSiluItems) {
     uint4 ga[kSiluItems], gb[kSiluItems], va[kSiluItems], vb[kSiluItems];
@@ -572,11 +598,23 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
       unpack16(va[u], vb[u], vw);
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[i] = bmul2(silu_lookup(tab, gw[i]), vw[i]);  // bf16(silu(g) * v)
-      uint32_t sb;
-      const uint2 codes = quantize16(y, gs, inv_gs, sb);
-      *reinterpret_cast<uint2 *>(p.q + row[u] * (p.K >> 1) + int64_t(grp[u]) * 8) = codes;
-      p.sf[sf_offset(row[u], grp[u], p.K)] = uint8_t(sb);
+      if constexpr (kAmax) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax_w = bmax2(amax_w, y[i] & kAbs2);
+      } else {
+        uint32_t sb;
+        const uint2 codes = quantize16(y, gs, inv_gs, sb);
+        *reinterpret_cast<uint2 *>(p.q + row[u] * (p.K >> 1) + int64_t(grp[u]) * 8) = codes;
+        p.sf[sf_offset(row[u], grp[u], p.K)] = uint8_t(sb);
+      }
     }
+  }
+  if constexpr (kAmax) {
+    float v = fmaxf(__uint_as_float(amax_w << 16), __uint_as_float(amax_w & 0xffff0000u));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned int *>(p.amax), __float_as_uint(v));  // v >= 0
+    return;
   }
   // zero scales of the padding rows M .. padded-1 (4 scale bytes per store)
   const int64_t pad_words = (p.padded - p.M) * (p.K / 64);
@@ -599,12 +637,14 @@ int64_t next_pow2(int64_t k) {
 
 using qe::fail;
 
-extern "C" {
-
-int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
-                      const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S,
-                      int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream) {
-  if (!x || !w || !noisy || !gs || !q || !sf) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: null argument");
+namespace qe {
+namespace {
+int norm_scale_impl(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
+                    const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S, int64_t K,
+                    int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, float *amax, void *stream) {
+  // with M = 0 the row buffers may be null (empty tensors)
+  if (!w || !noisy || (M > 0 && (!x || (!amax && (!gs || !q || !sf)))))
+    return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: null argument");
   if (mask && !clean) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: a token mask needs `clean` rows");
   if (mask && shift && !shift_clean)
     return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: a token mask with a shift needs `shift_clean` rows");
@@ -618,10 +658,14 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   if (mod_stride < 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: negative mod_stride");
   if (!qe::aligned16(x) || !qe::aligned16(w))
     return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: x and w must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(sf) & 3))
-    return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: q and sf must be 4-byte aligned");
-  const int64_t padded = qe::pad128(M);
-  if (padded == 0) return qe::ok();
+  if (!amax && ((reinterpret_cast<uintptr_t>(q) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3)))
+    return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: q must be 8-byte and sf 4-byte aligned");
+  const int64_t padded = amax ? M : qe::pad128(M);  // the pre-pass writes no padding scales
+  if (amax) {
+    cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(float), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return qe::cuda_status(e, "qe_norm_scale_amax: clear");
+  }
+  if (padded == 0) return 0;
   qe::NormParams p{};
   p.x = static_cast<const uint4 *>(x);
   p.w = static_cast<const uint4 *>(w);
@@ -639,6 +683,7 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   p.mod_stride = mod_stride;
   p.padded = padded;
   p.eps = eps;
+  p.amax = amax;
   const int64_t P = qe::next_pow2(K);
   p.leaf_len = P >= 128 ? 128 : int32_t(P);
   p.leaves = int32_t(P / p.leaf_len);
@@ -670,10 +715,28 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
   }
   if (best_warps == 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for two rows per warp");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int s = use_tables ? (has_shift ? qe::launch_norm_warps<true, true>(best_warps, p, best_smem, st)
-                                  : qe::launch_norm_warps<true, false>(best_warps, p, best_smem, st))
-                     : (has_shift ? qe::launch_norm_warps<false, true>(best_warps, p, best_smem, st)
-                                  : qe::launch_norm_warps<false, false>(best_warps, p, best_smem, st));
+  return amax ? qe::launch_norm<true>(use_tables, has_shift, best_warps, p, best_smem, st)
+              : qe::launch_norm<false>(use_tables, has_shift, best_warps, p, best_smem, st);
+}
+}  // namespace
+}  // namespace qe
+
+extern "C" {
+
+int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
+                      const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S,
+                      int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream) {
+  int s = qe::norm_scale_impl(x, w, noisy, clean, mask, shift, shift_clean, gs, M, S, K, mod_stride, eps, q, sf,
+                              nullptr, stream);
+  return s ? s : qe::ok();
+}
+
+int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
+                       const void *shift, const void *shift_clean, int64_t M, int64_t S, int64_t K,
+                       int64_t mod_stride, float eps, float *amax, void *stream) {
+  if (!amax) return fail(QE_ERR_INVALID, "qe_norm_scale_amax: null amax");
+  int s = qe::norm_scale_impl(x, w, noisy, clean, mask, shift, shift_clean, nullptr, M, S, K, mod_stride, eps,
+                              nullptr, nullptr, amax, stream);
   return s ? s : qe::ok();
 }
 
@@ -686,43 +749,72 @@ int qe_silu_table_init(uint16_t *table, void *stream) {
   return s ? s : qe::ok();
 }
 
-int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
-                    uint8_t *sf, const uint16_t *silu_table, void *stream) {
-  if (!gate || !value || !gs || !q || !sf || !silu_table)
+}  // extern "C"
+
+namespace qe {
+namespace {
+int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
+                  uint8_t *sf, const uint16_t *silu_table, float *amax, void *stream) {
+  // with M = 0 the row buffers may be null (empty tensors)
+  if (!silu_table || (M > 0 && (!gate || !value || (!amax && (!gs || !q || !sf)))))
     return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: null argument");
   if (M < 0 || K <= 0) return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: bad sizes");
   if (K % 64 != 0) return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: K=%lld must be a multiple of 64", (long long)K);
-  if (!qe::aligned16(gate) || !qe::aligned16(value) || !qe::aligned16(silu_table))
+  if (!aligned16(gate) || !aligned16(value) || !aligned16(silu_table))
     return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: gate, value and the table must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3))
+  if (!amax && ((reinterpret_cast<uintptr_t>(q) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3)))
     return fail(QE_ERR_INVALID, "qe_silu_mul_fp4: q must be 8-byte and sf 4-byte aligned");
-  const int64_t padded = qe::pad128(M);
-  if (padded == 0) return qe::ok();
-  qe::SiluParams p{};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (amax) {
+    cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(float), st);
+    if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_amax: clear");
+  }
+  const int64_t padded = pad128(M);
+  if (padded == 0) return 0;
+  SiluParams p{};
   p.gate = static_cast<const uint4 *>(gate);
   p.value = static_cast<const uint4 *>(value);
   p.gs = gs;
   p.table = reinterpret_cast<const uint4 *>(silu_table);
   p.q = q;
   p.sf = sf;
+  p.amax = amax;
   p.M = M;
   p.K = K;
   p.padded = padded;
-  constexpr size_t smem = size_t(qe::kSiluTable) * 2;
-  static bool attr_set[64] = {};
+  constexpr size_t smem = size_t(kSiluTable) * 2;
+  static bool attr_set[2][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qe::silu_mul_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return qe::cuda_status(e, "qe_silu_mul_fp4: smem attribute");
-    attr_set[dev] = true;
+  auto kernel = amax ? silu_mul_fp4_kernel<true> : silu_mul_fp4_kernel<false>;
+  if (!attr_set[amax ? 1 : 0][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_fp4: smem attribute");
+    attr_set[amax ? 1 : 0][dev] = true;
   }
   const int64_t items = M * ((K / 16 + 31) / 32);  // warp items: 32 groups of one row
-  const int64_t warps_per_block = qe::kSiluThreads / 32;
-  int64_t blocks = (std::max<int64_t>(items, (padded - M) * (K / 64) / 32) + warps_per_block - 1) / warps_per_block;
-  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(qe::sm_count())));
-  qe::silu_mul_fp4_kernel<<<dim3(unsigned(blocks)), dim3(qe::kSiluThreads), smem, static_cast<cudaStream_t>(stream)>>>(p);
-  int s = qe::cuda_status(cudaGetLastError(), "qe_silu_mul_fp4 launch");
+  const int64_t warps_per_block = kSiluThreads / 32;
+  const int64_t pad_items = amax ? 0 : (padded - M) * (K / 64) / 32;
+  int64_t blocks = (std::max<int64_t>(items, pad_items) + warps_per_block - 1) / warps_per_block;
+  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count())));
+  kernel<<<dim3(unsigned(blocks)), dim3(kSiluThreads), smem, st>>>(p);
+  return cuda_status(cudaGetLastError(), "qe_silu_mul_fp4 launch");
+}
+}  // namespace
+}  // namespace qe
+
+extern "C" {
+
+int qe_silu_mul_fp4(const void *gate, const void *value, const float *gs, int64_t M, int64_t K, uint8_t *q,
+                    uint8_t *sf, const uint16_t *silu_table, void *stream) {
+  int s = qe::silu_mul_impl(gate, value, gs, M, K, q, sf, silu_table, nullptr, stream);
+  return s ? s : qe::ok();
+}
+
+int qe_silu_mul_amax(const void *gate, const void *value, int64_t M, int64_t K, const uint16_t *silu_table,
+                     float *amax, void *stream) {
+  if (!amax) return fail(QE_ERR_INVALID, "qe_silu_mul_amax: null amax");
+  int s = qe::silu_mul_impl(gate, value, nullptr, M, K, nullptr, nullptr, silu_table, amax, stream);
   return s ? s : qe::ok();
 }
 

@@ -64,11 +64,25 @@ def _mod_rows(name: str, t: torch.Tensor | None, k: int) -> torch.Tensor | None:
     return t
 
 
-def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clean=None) -> Quantized:
-    """RMSNorm (``norm.weight``, ``norm.eps``) then the per-token adaLN scale, quantised to NVFP4 with global scale ``gs``.
+class _NormArgs(NamedTuple):
+    m: int
+    s: int
+    k: int
+    stride: int
+    weight: torch.Tensor
+    noisy: torch.Tensor
+    clean: torch.Tensor | None
+    mask: torch.Tensor | None
+    shift: torch.Tensor | None
+    shift_clean: torch.Tensor | None
 
-    Tokens whose ``noise_mask`` is true take ``noisy`` modulation, the others ``clean`` (fibo/dit.py:37-41).
-    """
+    def pointers(self, x):
+        ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        return (x.data_ptr(), self.weight.data_ptr(), self.noisy.data_ptr(), ptr(self.clean), ptr(self.mask),
+                ptr(self.shift), ptr(self.shift_clean))
+
+
+def _norm_args(x, norm, noisy, clean, noise_mask, shift, shift_clean) -> _NormArgs:
     _check_cuda_bf16("x", x)
     k = x.shape[-1]
     if k % 64:
@@ -76,7 +90,7 @@ def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clea
     if not x.is_contiguous():
         raise ValueError("x must be contiguous")
     s = x.shape[-2] if x.dim() >= 2 else x.shape[0]
-    m, padded, q, sf = _buffers(x, k)
+    m = x.numel() // k
     weight = norm.weight
     _check_cuda_bf16("norm.weight", weight)
     if weight.numel() != k or not weight.is_contiguous():
@@ -105,13 +119,42 @@ def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clea
         mask = noise_mask.contiguous().view(torch.uint8)
         if clean is None:
             raise ValueError("a noise mask needs clean modulation rows")
+    return _NormArgs(m, s, k, stride, weight, noisy, clean, mask, shift, shift_clean)
+
+
+def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clean=None) -> Quantized:
+    """RMSNorm (``norm.weight``, ``norm.eps``) then the per-token adaLN scale, quantised to NVFP4 with global scale ``gs``.
+
+    Tokens whose ``noise_mask`` is true take ``noisy`` modulation, the others ``clean`` (fibo/dit.py:37-41).
+    """
+    a = _norm_args(x, norm, noisy, clean, noise_mask, shift, shift_clean)
+    _, _, q, sf = _buffers(x, a.k)
     gs = _gs(gs, x.device)
-    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
     with torch.cuda.device(x.device):
-        _lib.call("qe_norm_scale_fp4", x.data_ptr(), weight.data_ptr(), noisy.data_ptr(), ptr(clean), ptr(mask),
-                  ptr(shift), ptr(shift_clean), gs.data_ptr(), m, s, k, stride, float(norm.eps), q.data_ptr(),
-                  sf.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        _lib.call("qe_norm_scale_fp4", *a.pointers(x), gs.data_ptr(), a.m, a.s, a.k, a.stride, float(norm.eps),
+                  q.data_ptr(), sf.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
     return Quantized(q, sf, x.shape)
+
+
+FP8_MAX, FP4_MAX = 448.0, 6.0
+
+
+def global_scale(amax: torch.Tensor, headroom: float = 4.0) -> torch.Tensor:
+    """Activation global scale from a calibration amax: ``448 * 6 / (max(amax, 1e-8) * headroom)`` in fp32
+    (pipeline/fp4.py:33-35, headroom env ``MULTI_TURN_NVFP4_HEADROOM``, default 4)."""
+    return (FP8_MAX * FP4_MAX / (amax.float().clamp(min=1e-8) * headroom)).to(torch.float32)
+
+
+def norm_scale_amax(x, norm, noisy, clean, noise_mask, shift=None, shift_clean=None) -> torch.Tensor:
+    """Calibration pre-pass of ``norm_scale_fp4``: max |y| (one-element fp32 device tensor) over the bf16 values
+    the quantiser would encode, in one launch with no bf16 tensor written. Replaces the reference's first-call
+    bf16 pass ``_norm_scale(...)`` + ``.float().abs().amax()`` (fibo/fp4.py:128-134, pipeline/fp4.py:33-35)."""
+    a = _norm_args(x, norm, noisy, clean, noise_mask, shift, shift_clean)
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("qe_norm_scale_amax", *a.pointers(x), a.m, a.s, a.k, a.stride, float(norm.eps), amax.data_ptr(),
+                  torch.cuda.current_stream(x.device).cuda_stream)
+    return amax
 
 
 _silu_tables: dict[int, torch.Tensor] = {}
@@ -130,24 +173,38 @@ def silu_table(device) -> torch.Tensor:
     return table
 
 
-def silu_mul_fp4(gate, value, gs, block=1024) -> Quantized:
-    """``silu(gate) * value`` quantised to NVFP4 (``block`` is accepted for signature parity and unused)."""
+def _silu_args(gate, value) -> tuple[int, int, torch.Tensor]:
     _check_cuda_bf16("gate", gate)
     _check_cuda_bf16("value", value)
     if gate.shape != value.shape:
         raise ValueError("gate and value must have the same shape")
     if not (gate.is_contiguous() and value.is_contiguous()):
         raise ValueError("gate and value must be contiguous")
+    if value.device != gate.device:
+        raise ValueError("gate and value on different devices")
     k = gate.shape[-1]
     if k % 64:
         raise ValueError(f"K={k} must be a multiple of 64")
-    m, padded, q, sf = _buffers(gate, k)
+    return gate.numel() // k, k, silu_table(gate.device)
+
+
+def silu_mul_fp4(gate, value, gs, block=1024) -> Quantized:
+    """``silu(gate) * value`` quantised to NVFP4 (``block`` is accepted for signature parity and unused)."""
+    m, k, table = _silu_args(gate, value)
+    _, _, q, sf = _buffers(gate, k)
     gs = _gs(gs, gate.device)
-    table = silu_table(gate.device)
     with torch.cuda.device(gate.device):
-        stream = torch.cuda.current_stream(gate.device)
-        if table.device != gate.device:
-            raise ValueError("silu table on another device")
         _lib.call("qe_silu_mul_fp4", gate.data_ptr(), value.data_ptr(), gs.data_ptr(), m, k, q.data_ptr(),
-                  sf.data_ptr(), table.data_ptr(), stream.cuda_stream)
+                  sf.data_ptr(), table.data_ptr(), torch.cuda.current_stream(gate.device).cuda_stream)
     return Quantized(q, sf, gate.shape)
+
+
+def silu_mul_amax(gate, value) -> torch.Tensor:
+    """Calibration pre-pass of ``silu_mul_fp4``: max |bf16(silu(gate) * value)| as a one-element fp32 device
+    tensor, in one launch with no bf16 product written (pipeline/fp4.py:33-35)."""
+    m, k, table = _silu_args(gate, value)
+    amax = torch.empty(1, dtype=torch.float32, device=gate.device)
+    with torch.cuda.device(gate.device):
+        _lib.call("qe_silu_mul_amax", gate.data_ptr(), value.data_ptr(), m, k, table.data_ptr(), amax.data_ptr(),
+                  torch.cuda.current_stream(gate.device).cuda_stream)
+    return amax

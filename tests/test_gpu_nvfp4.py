@@ -14,7 +14,8 @@ import pytest
 import torch
 
 from oracle import nvfp4_ref
-from qwenedit_b200.fp4 import Quantized, norm_scale_fp4, silu_mul_fp4, silu_table
+from qwenedit_b200.fp4 import (Quantized, global_scale, norm_scale_amax, norm_scale_fp4, silu_mul_amax, silu_mul_fp4,
+                               silu_table)
 from tests.golden import cases, inputs
 
 pytestmark = pytest.mark.gpu
@@ -140,3 +141,82 @@ def test_silu_table_is_exact_for_every_bf16_input():
     special = nan_in | neg_inf
     assert is_nan(table[special]).all() and is_nan(ref[special]).all()
     np.testing.assert_array_equal(table[~special], ref[~special])
+
+
+# ---- calibration pre-passes (amax of the exact bf16 y; pipeline/fp4.py:33-35, fibo/fp4.py:128-134) ----
+
+_ORACLE_SILU = None
+
+
+def _oracle_silu_y(gate, value):
+    """bf16(bf16(silu(g)) * v) with the oracle's SiLU (ref_silu_bf16 per bf16 bit pattern)."""
+    global _ORACLE_SILU
+    if _ORACLE_SILU is None:
+        _ORACLE_SILU = np.array([nvfp4_ref.lib().ref_silu_bf16(i) for i in range(65536)], np.uint16)
+    bits = gate.contiguous().view(torch.int16).numpy().view(np.uint16)
+    s = torch.from_numpy(_ORACLE_SILU[bits].view(np.int16)).view(torch.bfloat16).float()
+    return (s * value.float()).bfloat16()
+
+
+@pytest.mark.parametrize("B,S,K,masked,shift,shared", [
+    (1, 4096, 3072, False, False, False), (1, 1000, 3072, False, True, False), (3, 67, 4160, True, True, False),
+    (2, 129, 12288, True, False, False), (4, 33, 640, True, True, True), (1, 1, 64, False, False, False)])
+def test_norm_scale_amax_is_the_exact_max_of_y(B, S, K, masked, shift, shared):
+    seed = B * 7 + S + K
+    x = inputs.bf16(seed, (B, S, K), scale=2.0)
+    w = inputs.bf16(seed + 1, (K,), scale=0.02, shift=1.0)
+    rows = 1 if shared else B
+    scale = inputs.bf16(seed + 2, (rows, K), scale=0.1)
+    clean = inputs.bf16(seed + 3, (rows, K), scale=0.1) if masked else None
+    mask = torch.from_numpy(inputs.uniforms(seed + 4, S) < 0.5) if masked else None
+    sh = inputs.bf16(seed + 5, (rows, K), scale=0.1) if shift else None
+    sh_clean = inputs.bf16(seed + 6, (rows, K), scale=0.1) if (shift and masked) else None
+    y = nvfp4_ref.bf16_values_norm_scale(x, w, 1e-6, scale, clean, mask, sh, sh_clean)
+    to = lambda t: None if t is None else t.to(DEV)  # noqa: E731
+    norm = SimpleNamespace(weight=to(w), eps=1e-6)
+    amax = norm_scale_amax(to(x), norm, to(scale), to(clean), to(mask), shift=to(sh), shift_clean=to(sh_clean))
+    assert amax.dtype == torch.float32 and amax.shape == (1,)
+    assert amax.item() == y.float().abs().max().item()
+    # calibrate then quantise on the device: the codes equal the oracle's at the oracle's global scale
+    gs = global_scale(amax)
+    assert gs.item() == nvfp4_ref.global_scale(y)
+    out = norm_scale_fp4(to(x), norm, to(scale), to(clean), to(mask), gs, shift=to(sh), shift_clean=to(sh_clean))
+    q_ref, sf_ref = nvfp4_ref.norm_scale_fp4_ref(x, w, 1e-6, scale, clean, mask, gs.item(), sh, sh_clean)
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@pytest.mark.parametrize("M,K", [(4096, 12288), (300, 9536), (1, 64), (129, 640)])
+def test_silu_mul_amax_is_the_exact_max_of_y(M, K):
+    gate = inputs.bf16(M + K + 2, (1, M, K), scale=3.0)
+    value = inputs.bf16(M + K + 3, (1, M, K))
+    y = _oracle_silu_y(gate, value)
+    amax = silu_mul_amax(gate.to(DEV), value.to(DEV))
+    assert amax.item() == y.float().abs().max().item()
+    gs = global_scale(amax)
+    assert gs.item() == nvfp4_ref.global_scale(y)
+    out = silu_mul_fp4(gate.to(DEV), value.to(DEV), gs)
+    q_ref, sf_ref = nvfp4_ref.silu_mul_fp4_ref(gate, value, gs.item())
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+def test_amax_edge_cases():
+    """Empty input gives 0 (and the clamped scale 448*6/(1e-8*4)); zeros give 0; each call clears the previous
+    result; a single large outlier anywhere is found."""
+    z = torch.zeros(0, 64, dtype=torch.bfloat16, device=DEV)
+    assert silu_mul_amax(z, z).item() == 0.0
+    assert global_scale(silu_mul_amax(z, z)).item() == nvfp4_ref.global_scale(torch.zeros(1))
+    zeros = torch.zeros(1, 256, 128, dtype=torch.bfloat16, device=DEV)
+    norm = SimpleNamespace(weight=torch.ones(128, dtype=torch.bfloat16, device=DEV), eps=1e-6)
+    mods = torch.zeros(1, 128, dtype=torch.bfloat16, device=DEV)
+    assert norm_scale_amax(zeros, norm, mods, None, None).item() == 0.0
+    gate = inputs.bf16(91, (1, 777, 192))
+    value = inputs.bf16(92, (1, 777, 192))
+    value[0, 555, 17] = -2.0e4
+    gate[0, 555, 17] = 20.0
+    y = _oracle_silu_y(gate, value)
+    g, v = gate.to(DEV), value.to(DEV)
+    first = silu_mul_amax(g, v).item()
+    assert first == y.float().abs().max().item() and first > 1e5
+    assert silu_mul_amax(g[:, :500], v[:, :500]).item() == y[:, :500].float().abs().max().item()
