@@ -391,22 +391,25 @@ def extras(pool, sess, device):
     del big
     torch.cuda.empty_cache()
     out.update(nvfp4_extras(device, peak))
+    out["nvfp4_cpu_baseline"] = nvfp4_cpu()
     return out
 
 
-def _time_kernel(fn, flush, iters=10):
+def _time_kernel(fn, flush, iters=20):
+    """Median CUDA-event time of `fn` over `iters` launches after 3 warm-ups, L2 flushed before each."""
     times = []
     for i in range(iters + 3):
         if flush is not None:
             flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(100_000)  # keeps the GPU busy while the host enqueues `fn`: no host time in the span
         a.record()
         fn()
         b.record()
         torch.cuda.synchronize()
         if i >= 3:
             times.append(a.elapsed_time(b))
-    return statistics.mean(times)
+    return statistics.median(times)
 
 
 def nvfp4_extras(device, peak):
@@ -448,6 +451,66 @@ def nvfp4_extras(device, peak):
             nbytes = 2 * T * K * 2
             out[f"silu_mul_amax_T{T}"] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
                                           "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4)}
+    return out
+
+
+def nvfp4_cpu(rows_norm: int = 8192, rows_silu: int = 1024):
+    """NVFP4 producers on the host cores: the oracle's C restatement of the reference kernels (scalar code,
+    one 128-row-aligned chunk of rows per thread). Returns GB/s at the kernels' algorithmic bytes."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import nvfp4_ref
+
+    lib = nvfp4_ref.lib()
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+
+    def bf16_bits(shape, scale=1.0, shift=0.0):
+        v = torch.from_numpy((rng.standard_normal(shape) * scale + shift).astype(np.float32)).bfloat16()
+        return v.view(torch.int16).numpy().view(np.uint16).copy()
+
+    def run(M, K, row_fn):
+        chunk = max(128, -(-M // threads) // 128 * 128)
+        starts = list(range(0, M, chunk))
+        with ThreadPoolExecutor(len(starts)) as ex:
+            t0 = time.perf_counter()
+            list(ex.map(lambda r0: row_fn(r0, min(chunk, M - r0)), starts))
+            return time.perf_counter() - t0, len(starts)
+
+    out = {}
+    K = 3072
+    x, w = bf16_bits((rows_norm, K)), bf16_bits((K,), 0.02, 1.0)
+    mod, sh = bf16_bits((1, K), 0.1), bf16_bits((1, K), 0.1)
+    q = np.zeros((rows_norm, K // 2), np.uint8)
+    sf = np.zeros((rows_norm, K // 16), np.uint8)
+    tile_sf = K // 64 * 512
+
+    def norm_rows(r0, n):
+        scratch = np.zeros(2 * 4096, np.float32)
+        p = lambda a, off=0: a.ctypes.data + off  # noqa: E731
+        lib.ref_norm_scale_fp4(p(x, r0 * K * 2), p(w), p(mod), None, None, p(sh), None, 50.0, n, n, K, 0, 1e-6,
+                               p(q, r0 * K // 2), p(sf, r0 // 128 * tile_sf), p(scratch))
+
+    sec, used = run(rows_norm, K, norm_rows)
+    nbytes = rows_norm * K * 2 + K * 2 * 3 + rows_norm * K // 2 + rows_norm * K // 16
+    out["norm_scale_fp4"] = {"GB/s": round(nbytes / sec / 1e9, 3), "sample": f"x [{rows_norm}, {K}]"}
+    K = 12288
+    g, v = bf16_bits((rows_silu, K)), bf16_bits((rows_silu, K))
+    q = np.zeros((rows_silu, K // 2), np.uint8)
+    sf = np.zeros((rows_silu, K // 16), np.uint8)
+    tile_sf = K // 64 * 512
+
+    def silu_rows(r0, n):
+        scratch = np.zeros(K, np.float32)
+        p = lambda a, off=0: a.ctypes.data + off  # noqa: E731
+        lib.ref_silu_mul_fp4(p(g, r0 * K * 2), p(v, r0 * K * 2), 50.0, n, K, p(q, r0 * K // 2),
+                             p(sf, r0 // 128 * tile_sf), p(scratch))
+
+    sec, used2 = run(rows_silu, K, silu_rows)
+    nbytes = 2 * rows_silu * K * 2 + rows_silu * K // 2 + rows_silu * K // 16
+    out["silu_mul_fp4"] = {"GB/s": round(nbytes / sec / 1e9, 3), "sample": f"gate, value [{rows_silu}, {K}]"}
+    out.update({"cores": max(used, used2), "kind": "port",
+                "what": "oracle C restatement of the reference kernels, 128-row chunks across threads"})
     return out
 
 

@@ -119,11 +119,6 @@ __device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
   asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
 // Four f32x2 pairs -> eight e2m1 codes in one word (pair i in byte i, its low element in the low nibble):
 // round to nearest even on {0, .5, 1, 1.5, 2, 3, 4, 6}, saturating, sign in bit 3. These are exactly the
 // reference's thresholds {>0.25, >=0.75, >1.25, >=1.75, >2.5, >=3.5, >5}; callers pass +0.0 for a -0.0
@@ -200,16 +195,37 @@ __device__ __forceinline__ int64_t sf_offset(int64_t m, int64_t g, int64_t K) {
 constexpr uint32_t kAbs2 = 0x7fff7fffu;
 constexpr uint32_t kOne2 = 0x3f803f80u;  // bf16x2 (1.0, 1.0)
 
+// max(|a|, |b|) per half; the sign bit it leaves (the XOR of the inputs' signs) is masked off by the caller
+__device__ __forceinline__ uint32_t bamax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// bf16x2 word whose halves are both max |y| over the 16 values of a group
+__device__ __forceinline__ uint32_t absmax16(const uint32_t (&y)[8]) {
+  const uint32_t a = bamax2(y[0], y[1]), b = bamax2(y[2], y[3]), c = bamax2(y[4], y[5]), d = bamax2(y[6], y[7]);
+  const uint32_t m = bamax2(bamax2(a, b), bamax2(c, d));
+  return bamax2(m, __byte_perm(m, 0, 0x1032)) & kAbs2;
+}
+
+// The reciprocal scale the quantiser multiplies by, for every e4m3 scale byte sb:
+// 1 / (e4m3(sb) * (1 / gs)), or 0 for a zero scale (fibo/fp4.py:53-55). 256 floats, built per CTA.
+constexpr int kScaleTab = 256;
+__device__ __forceinline__ void build_scale_table(float *tab, float inv_gs) {
+  for (int b = threadIdx.x; b < kScaleTab; b += blockDim.x) {
+    const float sff = e4m3_value(uint32_t(b));
+    tab[b] = sff != 0.0f ? __frcp_rn(__fmul_rn(sff, inv_gs)) : 0.0f;
+  }
+}
+
 // Quantise one 16-value group held as 8 bf16x2 words: returns the 16 codes as 8 bytes (two words, the even
 // column of each pair in the low nibble) and the group's e4m3 scale byte (fibo/fp4.py:46-61).
-__device__ __forceinline__ uint2 quantize16(const uint32_t (&y)[8], float gs, float inv_gs, uint32_t &sb) {
-  const uint32_t m01 = bmax2(y[0] & kAbs2, y[1] & kAbs2), m23 = bmax2(y[2] & kAbs2, y[3] & kAbs2);
-  const uint32_t m45 = bmax2(y[4] & kAbs2, y[5] & kAbs2), m67 = bmax2(y[6] & kAbs2, y[7] & kAbs2);
-  const uint32_t m = bmax2(bmax2(m01, m23), bmax2(m45, m67));
-  const float amax = fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
+__device__ __forceinline__ uint2 quantize16(const uint32_t (&y)[8], float gs, const float *scale_tab,
+                                            uint32_t &sb) {
+  const float amax = __uint_as_float(absmax16(y) << 16);
   sb = e4m3_byte(__fmul_rn(gs, __fmul_rn(amax, 0.16666667163372039795f)));
-  const float sff = e4m3_value(sb);
-  const float scale = sff != 0.0f ? __frcp_rn(__fmul_rn(sff, inv_gs)) : 0.0f;
+  const float scale = scale_tab[sb];
   const f32x2 scale2 = pk2(scale, scale), zero2 = pk2(0.0f, 0.0f);
   f32x2 v[8];
 #pragma unroll
@@ -300,35 +316,54 @@ inline size_t norm_table_bytes(int64_t K, int64_t rows, bool shift) {
   return size_t(K) * 2 * size_t(1 + rows * (shift ? 2 : 1));
 }
 
+constexpr int pow2_at_least(int k) { return k <= 1 ? 1 : 2 * pow2_at_least((k + 1) / 2); }
+
 // One warp per row, rows strided over the grid. Each warp owns two row buffers in shared memory: while it
 // quantises row m from one, cp.async streams its next row into the other. With kTables the CTA first stages
 // the per-column constants (w, the pre-rounded bf16(1 + scale) rows of every batch and mask variant, the
 // shift rows) in shared memory, so the per-row work reads them from there; without, they come from global
 // memory. In the element-wise pass lane l owns the 16-value groups g = l + 32 i.
+// kK != 0 specialises the row width at compile time (every per-row loop unrolled, swizzled addresses
+// hoisted out of the row loop); kK == 0 reads K from the parameters.
 // kAmax: the calibration pre-pass — the same y, reduced to max |y| instead of quantised and stored.
-template <int kWarps, bool kTables, bool kShift, bool kAmax>
+template <int kK, int kWarps, bool kTables, bool kShift, bool kAmax>
 __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams p) {
   extern __shared__ uint4 smem[];
+  constexpr int kP = kK ? pow2_at_least(kK) : 0;
+  constexpr int kLeafLen = kP >= 128 ? 128 : kP;
+  const int K = kK ? kK : int(p.K);
+  const int leaf_len = kK ? kLeafLen : p.leaf_len;
+  const int leaves = kK ? kP / kLeafLen : p.leaves;
+  const int row_chunks = kK ? (kK + 127) / 128 * 16 : p.row_chunks;
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
-  const int gpr = int(p.K >> 4);  // 16-value groups per row
-  const int kc = int(p.K >> 3);   // 16-byte chunks per row
-  const int half = gpr;           // group-interleaved table: second chunks start here
+  const int gpr = K >> 4;  // 16-value groups per row
+  const int kc = K >> 3;   // 16-byte chunks per row
+  const int half = gpr;    // group-interleaved table: second chunks start here
   const int mod_rows = p.batches * p.variants;
-  uint4 *w_s = smem;
+  float *scale_tab = reinterpret_cast<float *>(smem);
+  uint4 *w_s = smem + kScaleTab / 4;
   uint4 *m1_s = w_s + (kTables ? kc : 0);
   uint4 *sh_s = m1_s + (kTables ? kc * mod_rows : 0);
-  uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + int64_t(wid) * 2 * p.row_chunks;
+  uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + wid * 2 * row_chunks;
   const int64_t warp0 = int64_t(blockIdx.x) * kWarps + wid;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
-  const float inv_gs = __fdiv_rn(1.0f, gs);
-  const float kf = float(p.K);
+  const float kf = float(K);
+  if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
 
   auto fetch = [&](int64_t row, uint4 *dst) {  // issue the async copy of one row (no-op past M)
     if (row < p.M) {
-      const uint4 *src = p.x + row * (p.K >> 3);
-      for (int c = lane; c < kc; c += 32) cp_async16(dst + swz(c), src + c);
+      const uint4 *src = p.x + row * kc;
+      if (kK) {
+#pragma unroll
+        for (int j = 0; j < (kK / 8 + 31) / 32; ++j) {
+          const int c = lane + 32 * j;
+          if ((kK / 8) % 32 == 0 || c < kc) cp_async16(dst + swz(c), src + c);
+        }
+      } else {
+        for (int c = lane; c < kc; c += 32) cp_async16(dst + swz(c), src + c);
+      }
     }
     cp_async_commit();
   };
@@ -338,7 +373,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   if (kTables) {
     for (int c = threadIdx.x; c < kc; c += kWarps * 32) w_s[gix(c, half)] = __ldg(p.w + c);
     for (int t = 0; t < mod_rows; ++t) {
-      const int64_t b = t / p.variants;
+      const int b = t / p.variants;
       const bool noisy = (t % p.variants) == 0;
       const __nv_bfloat16 *mrow = (noisy ? p.noisy : p.clean) + b * p.mod_stride;
       const __nv_bfloat16 *srow = kShift ? (noisy ? p.shift : p.shift_clean) + b * p.mod_stride : nullptr;
@@ -354,53 +389,78 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
         }
       }
     }
-    __syncthreads();
   }
+  __syncthreads();  // scale table (and constant tables) visible to every warp
+
+  // row m = b * S + s; b, s and b % batches advance by fixed steps instead of dividing per row
+  const int S = int(p.S);
+  int b = int(warp0 / S), s = int(warp0 % S), bb = b % p.batches;
+  const int db = int(nwarps / S), ds = int(nwarps % S), dbb = db % p.batches;
+  auto advance = [&]() {
+    s += ds;
+    b += db;
+    bb += dbb;
+    if (s >= S) {
+      s -= S;
+      ++b;
+      ++bb;
+    }
+    if (bb >= p.batches) bb -= p.batches;
+  };
+  // chunk index of x chunk 2g (g = lane + 32 i) inside a row buffer: swz(2 (lane + 32 i)) written out
+  const int x_lane = ((lane >> 3) << 4) + ((2 * lane & 15) ^ (lane >> 3) ^ ((lane >> 2) & 1));
 
   int cur = 0;
-  for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1) {
-    fetch(m + nwarps, bufs + (cur ^ 1) * p.row_chunks);
+  for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1, advance()) {
+    fetch(m + nwarps, bufs + (cur ^ 1) * row_chunks);
     cp_async_wait_1();  // this row's copies (all but the newest group) have landed
     __syncwarp();
     if (m >= p.M) {  // padding rows of the last 128-row tile: zero scales, no codes
-      if (!kAmax) zero_sf_row(p.sf, m, p.K, lane);
+      if (!kAmax) zero_sf_row(p.sf, m, K, lane);
       __syncwarp();
       continue;
     }
-    const uint4 *row_s = bufs + cur * p.row_chunks;
+    const uint4 *row_s = bufs + cur * row_chunks;
 
     // sum of squares, numpy pairwise order: leaf j = elements [leaf_len*j, leaf_len*j + leaf_len); lane l
     // owns leaves l, l+32, l+64, l+96; each round's 32 leaves reduce by a butterfly (a balanced tree), and
     // the rounds (halves / quarters of the padded block) combine as a balanced tree
-    const int rounds = p.leaves > 32 ? p.leaves / 32 : 1;  // 1, 2 or 4
+    const int rounds = leaves > 32 ? leaves / 32 : 1;  // 1, 2 or 4
     float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       if (r < rounds) {
         const int leaf = lane + 32 * r;
-        float s = 0.0f;
-        if (leaf < p.leaves && leaf * p.leaf_len < p.K) {
+        float sum = 0.0f;
+        if (leaf < leaves && leaf * leaf_len < K) {
           // eight running sums (element 8c + e goes to sum e); the first chunk seeds them (0 + x*x = x*x)
-          float r[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-          const int nchunk = min(p.leaf_len / 8, int((p.K - int64_t(leaf) * p.leaf_len) / 8));
-          for (int c = 0; c < nchunk; ++c) {
-            const uint4 v = row_s[swz((leaf << 4) | c)];
-            sq_acc2(v.x, r[0], r[1]);
-            sq_acc2(v.y, r[2], r[3]);
-            sq_acc2(v.z, r[4], r[5]);
-            sq_acc2(v.w, r[6], r[7]);
+          float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+          const int nchunk = min(leaf_len / 8, (K - leaf * leaf_len) / 8);
+          const uint4 *leaf_s = row_s + (leaf << 4);
+          const int key = leaf & 15;  // swz inside a leaf: chunk c sits at c ^ key ^ (c >> 3 & 1)
+          auto chunk = [&](int c) {
+            const uint4 v = leaf_s[c ^ key ^ ((c >> 3) & 1)];
+            sq_acc2(v.x, acc[0], acc[1]);
+            sq_acc2(v.y, acc[2], acc[3]);
+            sq_acc2(v.z, acc[4], acc[5]);
+            sq_acc2(v.w, acc[6], acc[7]);
+          };
+          if (nchunk == 16) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) chunk(c);
+          } else {
+            for (int c = 0; c < nchunk; ++c) chunk(c);
           }
           // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7))
-          const float2 a0 = make_float2(r[0], r[1]), a1 = make_float2(r[2], r[3]);
-          const float2 a2 = make_float2(r[4], r[5]), a3 = make_float2(r[6], r[7]);
-          const float2 t = up2(add2(pk2(a0.x, a2.x), pk2(a0.y, a2.y)));
-          const float2 u2 = up2(add2(pk2(a1.x, a3.x), pk2(a1.y, a3.y)));
-          const float2 v2 = up2(add2(pk2(t.x, t.y), pk2(u2.x, u2.y)));
-          s = __fadd_rn(v2.x, v2.y);
+          const f32x2 t = add2(pk2(acc[0], acc[2]), pk2(acc[1], acc[3]));
+          const f32x2 u2 = add2(pk2(acc[4], acc[6]), pk2(acc[5], acc[7]));
+          const float2 tt = up2(t), uu = up2(u2);
+          const float2 v2 = up2(add2(pk2(tt.x, uu.x), pk2(tt.y, uu.y)));
+          sum = __fadd_rn(v2.x, v2.y);
         }
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-        part[r] = s;
+        for (int off = 1; off < 32; off <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+        part[r] = sum;
       }
     }
     const float total = rounds == 1   ? part[0]
@@ -409,21 +469,20 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, kf), p.eps)));
     const f32x2 rstd2 = pk2(rstd, rstd);
 
-    const int64_t b = m / p.S;
-    const bool use_noisy = p.mask == nullptr || __ldg(p.mask + (m % p.S)) != 0;
-    const int t = int(b % p.batches) * p.variants + (use_noisy ? 0 : 1);  // batches == 1: one shared row
+    const bool use_noisy = p.mask == nullptr || __ldg(p.mask + s) != 0;
+    const int t = bb * p.variants + (use_noisy ? 0 : 1);  // batches == 1: one shared row
     const uint4 *m1_row = m1_s + t * kc;
     const uint4 *sh_row_s = sh_s + t * kc;
-    const __nv_bfloat16 *mod_row = (use_noisy ? p.noisy : p.clean) + b * p.mod_stride;
+    const __nv_bfloat16 *mod_row = (use_noisy ? p.noisy : p.clean) + int64_t(b) * p.mod_stride;
     const __nv_bfloat16 *sh_base = use_noisy ? p.shift : p.shift_clean;
-    const __nv_bfloat16 *sh_row = kShift ? sh_base + b * p.mod_stride : nullptr;
-    uint8_t *q_row = p.q + m * (p.K >> 1);
+    const __nv_bfloat16 *sh_row = kShift ? sh_base + int64_t(b) * p.mod_stride : nullptr;
+    uint8_t *q_row = p.q + m * (K >> 1);
     // scale-byte offset = row part + group part (fibo/fp4.py:60)
-    const int64_t sf_row = (m >> 7) * (p.K / 64 * 512) + (m & 31) * 16 + ((m & 127) >> 5) * 4;
+    const int64_t sf_row = (m >> 7) * (K / 64 * 512) + (m & 31) * 16 + ((m & 127) >> 5) * 4;
 
-    auto group = [&](int g) {
+    auto group = [&](int g, int xi) {  // xi: chunk index of x chunk 2g in the row buffer
       uint32_t xu[8], wu[8], mv[8], sv[8];
-      unpack16(row_s[swz(2 * g)], row_s[swz(2 * g + 1)], xu);
+      unpack16(row_s[xi], row_s[xi ^ 1], xu);
       if (kTables) {
         unpack16(w_s[g], w_s[half + g], wu);
         unpack16(m1_row[g], m1_row[half + g], mv);
@@ -452,24 +511,34 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
       }
       if constexpr (kAmax) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax_w = bmax2(amax_w, y[i] & kAbs2);
+        for (int i = 0; i < 8; ++i) amax_w = bamax2(amax_w, y[i]);
       } else {
         uint32_t sb;
-        const uint2 codes = quantize16(y, gs, inv_gs, sb);
+        const uint2 codes = quantize16(y, gs, scale_tab, sb);
         *reinterpret_cast<uint2 *>(q_row + g * 8) = codes;
         p.sf[sf_row + (g >> 2) * 512 + (g & 3)] = uint8_t(sb);
       }
     };
-    int g = lane;
-    for (; g + 32 < gpr; g += 64) {  // two independent groups per iteration
-      group(g);
-      group(g + 32);
+    if (kK) {
+      // g = lane + 32 i: chunk 2g is at x_lane + 64 i with the swizzle key's bits 2-3 advanced by i
+#pragma unroll
+      for (int i = 0; i < (kK / 16 + 31) / 32; ++i) {
+        const int g = lane + 32 * i;
+        if ((kK / 16) % 32 == 0 || g < gpr) group(g, (x_lane + 64 * i) ^ (4 * (i & 3)));
+      }
+    } else {
+      int g = lane;
+      for (; g + 32 < gpr; g += 64) {  // two independent groups per iteration
+        group(g, swz(2 * g));
+        group(g + 32, swz(2 * g + 64));
+      }
+      if (g < gpr) group(g, swz(2 * g));
     }
-    if (g < gpr) group(g);
     __syncwarp();  // every lane is done with this buffer before it is refilled
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   if constexpr (kAmax) {
+    amax_w &= kAbs2;
     float v = fmaxf(__uint_as_float(amax_w << 16), __uint_as_float(amax_w & 0xffff0000u));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -477,9 +546,9 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   }
 }
 
-template <int kWarps, bool kTables, bool kShift, bool kAmax>
+template <int kK, int kWarps, bool kTables, bool kShift, bool kAmax>
 int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
-  auto kernel = norm_scale_fp4_kernel<kWarps, kTables, kShift, kAmax>;
+  auto kernel = norm_scale_fp4_kernel<kK, kWarps, kTables, kShift, kAmax>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -497,23 +566,31 @@ int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
 }
 
-template <bool kTables, bool kShift, bool kAmax>
+template <int kK, bool kTables, bool kShift, bool kAmax>
 int launch_norm_warps(int warps, const NormParams &p, size_t smem, cudaStream_t stream) {
   switch (warps) {
-    case 16: return launch_norm_typed<16, kTables, kShift, kAmax>(p, smem, stream);
-    case 8: return launch_norm_typed<8, kTables, kShift, kAmax>(p, smem, stream);
-    case 6: return launch_norm_typed<6, kTables, kShift, kAmax>(p, smem, stream);
-    case 4: return launch_norm_typed<4, kTables, kShift, kAmax>(p, smem, stream);
-    default: return launch_norm_typed<2, kTables, kShift, kAmax>(p, smem, stream);
+    case 16: return launch_norm_typed<kK, 16, kTables, kShift, kAmax>(p, smem, stream);
+    case 8: return launch_norm_typed<kK, 8, kTables, kShift, kAmax>(p, smem, stream);
+    case 6: return launch_norm_typed<kK, 6, kTables, kShift, kAmax>(p, smem, stream);
+    case 4: return launch_norm_typed<kK, 4, kTables, kShift, kAmax>(p, smem, stream);
+    default: return launch_norm_typed<kK, 2, kTables, kShift, kAmax>(p, smem, stream);
   }
 }
 
+template <int kK, bool kAmax>
+int launch_norm_k(bool tables, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
+  return tables ? (shift ? launch_norm_warps<kK, true, true, kAmax>(warps, p, smem, st)
+                         : launch_norm_warps<kK, true, false, kAmax>(warps, p, smem, st))
+                : (shift ? launch_norm_warps<kK, false, true, kAmax>(warps, p, smem, st)
+                         : launch_norm_warps<kK, false, false, kAmax>(warps, p, smem, st));
+}
+
+// Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
+// multiple of 64 takes the runtime-K kernel.
 template <bool kAmax>
 int launch_norm(bool tables, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
-  return tables ? (shift ? launch_norm_warps<true, true, kAmax>(warps, p, smem, st)
-                         : launch_norm_warps<true, false, kAmax>(warps, p, smem, st))
-                : (shift ? launch_norm_warps<false, true, kAmax>(warps, p, smem, st)
-                         : launch_norm_warps<false, false, kAmax>(warps, p, smem, st));
+  if (p.K == 3072) return launch_norm_k<3072, kAmax>(tables, shift, warps, p, smem, st);
+  return launch_norm_k<0, kAmax>(tables, shift, warps, p, smem, st);
 }
 
 // ---- SiLU(gate) * value -> NVFP4 ---------------------------------------------------------------
@@ -559,7 +636,10 @@ __device__ __forceinline__ uint32_t silu_lookup(const uint16_t *tab, uint32_t w)
 template <bool kAmax>
 __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
   extern __shared__ uint4 tab4[];
+  float *scale_tab = reinterpret_cast<float *>(tab4 + kSiluTable / 8);
   for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
+  const float gs = kAmax ? 1.0f : __ldg(p.gs);
+  if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
   __syncthreads();
   const uint16_t *tab = reinterpret_cast<const uint16_t *>(tab4);
   const int lane = threadIdx.x & 31;
@@ -568,8 +648,6 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
   const int64_t items = p.M * segs;
   const int64_t warp = (int64_t(blockIdx.x) * kSiluThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * kSiluThreads) >> 5;
-  const float gs = kAmax ? 1.0f : __ldg(p.gs);
-  const float inv_gs = __fdiv_rn(1.0f, gs);
   uint32_t amax_w = 0u;  // kAmax: running bf16x2 max of |y|
 
   for (int64_t it0 = warp; it0 < items; it0 += nwarps * kSiluItems) {
@@ -600,16 +678,17 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
       for (int i = 0; i < 8; ++i) y[i] = bmul2(silu_lookup(tab, gw[i]), vw[i]);  // bf16(silu(g) * v)
       if constexpr (kAmax) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax_w = bmax2(amax_w, y[i] & kAbs2);
+        for (int i = 0; i < 8; ++i) amax_w = bamax2(amax_w, y[i]);
       } else {
         uint32_t sb;
-        const uint2 codes = quantize16(y, gs, inv_gs, sb);
+        const uint2 codes = quantize16(y, gs, scale_tab, sb);
         *reinterpret_cast<uint2 *>(p.q + row[u] * (p.K >> 1) + int64_t(grp[u]) * 8) = codes;
         p.sf[sf_offset(row[u], grp[u], p.K)] = uint8_t(sb);
       }
     }
   }
   if constexpr (kAmax) {
+    amax_w &= kAbs2;
     float v = fmaxf(__uint_as_float(amax_w << 16), __uint_as_float(amax_w & 0xffff0000u));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -655,6 +734,7 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   if (!qe::aligned16(x)) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: x must be 16-byte aligned");
   if (M % S != 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: M=%lld is not a multiple of S=%lld",
                                (long long)M, (long long)S);
+  if (M > (int64_t(1) << 30)) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: M=%lld above 2^30 rows", (long long)M);
   if (mod_stride < 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: negative mod_stride");
   if (!qe::aligned16(x) || !qe::aligned16(w))
     return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: x and w must be 16-byte aligned");
@@ -704,7 +784,7 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   int best_warps = 0, best_resident = 0;
   size_t best_smem = 0;
   for (int w : {16, 8, 6, 4, 2}) {
-    const size_t smem = size_t(w) * row_pair + (use_tables ? tables : 0);
+    const size_t smem = qe::kScaleTab * sizeof(float) + size_t(w) * row_pair + (use_tables ? tables : 0);
     if (smem > kSmemMax) continue;
     const int per_sm = std::min<int>(int(kSmemMax / smem), 32 / w);
     if (per_sm * w > best_resident) {
@@ -782,7 +862,7 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.M = M;
   p.K = K;
   p.padded = padded;
-  constexpr size_t smem = size_t(kSiluTable) * 2;
+  constexpr size_t smem = size_t(kSiluTable) * 2 + kScaleTab * sizeof(float);
   static bool attr_set[2][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
