@@ -48,6 +48,7 @@ SIGNATURES: dict[str, list] = {
                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
     "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "qe_silu_table_init": [c_void_p, c_void_p],
+    "qe_set_norm_table_mode": [c_int32],
     "qe_norm_scale_amax": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p],
     "qe_silu_mul_amax": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],

@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "qe_cuda.cuh"
@@ -318,16 +319,81 @@ inline size_t norm_table_bytes(int64_t K, int64_t rows, bool shift) {
 
 constexpr int pow2_at_least(int k) { return k <= 1 ? 1 : 2 * pow2_at_least((k + 1) / 2); }
 
+// ---- tensor memory (TMEM) as per-lane constant storage -----------------------------------------
+// With the row width fixed at compile time, lane l of every warp reads the same per-column constants (those of
+// its groups g = l + 32 i) for every row. They are written once per CTA into TMEM lane l of each 32-lane
+// quarter and read back with tcgen05.ld, which keeps them off the shared-memory data path that the row
+// buffers use. A warp w can only address TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31.
+constexpr uint32_t kTmemCols = 256;  // allocation per CTA (at most two such CTAs share an SM's 512 columns)
+// scale table, then a 128-byte slot holding the TMEM address (keeps the row buffers 128-byte aligned, which
+// their bank-conflict-free swizzle relies on)
+constexpr int kHeadUint4 = kScaleTab / 4 + 8;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// whole warp: allocate kTmemCols columns, write the TMEM address to *slot, give up further allocations
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(kTmemCols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTmemCols) : "memory");
+}
+__device__ __forceinline__ void tmem_fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 8 consecutive columns at a and at b (this thread's lane), waited for inside the same statement so that no
+// instruction can read the registers before they are written
+__device__ __forceinline__ void tmem_ld8x2(uint32_t a, uint32_t b, uint32_t (&x)[8], uint32_t (&y)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%16];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%17];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
+        "=r"(y[0]), "=r"(y[1]), "=r"(y[2]), "=r"(y[3]), "=r"(y[4]), "=r"(y[5]), "=r"(y[6]), "=r"(y[7])
+      : "r"(a), "r"(b)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld8x3(uint32_t a, uint32_t b, uint32_t c, uint32_t (&x)[8], uint32_t (&y)[8],
+                                           uint32_t (&z)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%24];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%25];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [%26];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
+        "=r"(y[0]), "=r"(y[1]), "=r"(y[2]), "=r"(y[3]), "=r"(y[4]), "=r"(y[5]), "=r"(y[6]), "=r"(y[7]),
+        "=r"(z[0]), "=r"(z[1]), "=r"(z[2]), "=r"(z[3]), "=r"(z[4]), "=r"(z[5]), "=r"(z[6]), "=r"(z[7])
+      : "r"(a), "r"(b), "r"(c)
+      : "memory");
+}
+
 // One warp per row, rows strided over the grid. Each warp owns two row buffers in shared memory: while it
-// quantises row m from one, cp.async streams its next row into the other. With kTables the CTA first stages
-// the per-column constants (w, the pre-rounded bf16(1 + scale) rows of every batch and mask variant, the
-// shift rows) in shared memory, so the per-row work reads them from there; without, they come from global
-// memory. In the element-wise pass lane l owns the 16-value groups g = l + 32 i.
+// quantises row m from one, cp.async streams its next row into the other. The per-column constants (w, the
+// pre-rounded bf16(1 + scale) rows of every batch and mask variant, the shift rows) come from global memory
+// (kTab 0), from tables the CTA stages in shared memory (kTab 1), or from TMEM (kTab 2, compile-time K only).
+// In the element-wise pass lane l owns the 16-value groups g = l + 32 i.
 // kK != 0 specialises the row width at compile time (every per-row loop unrolled, swizzled addresses
 // hoisted out of the row loop); kK == 0 reads K from the parameters.
 // kAmax: the calibration pre-pass — the same y, reduced to max |y| instead of quantised and stored.
-template <int kK, int kWarps, bool kTables, bool kShift, bool kAmax>
+template <int kK, int kWarps, int kTab, bool kShift, bool kAmax>
 __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams p) {
+  static_assert(kTab != 2 || (kK != 0 && (kK / 16) % 32 == 0 && kWarps >= 4),
+                "TMEM tables need a compile-time K of whole 512-column blocks and four warps");
+  constexpr bool kTables = kTab == 1;
+  constexpr bool kTmem = kTab == 2;
   extern __shared__ uint4 smem[];
   constexpr int kP = kK ? pow2_at_least(kK) : 0;
   constexpr int kLeafLen = kP >= 128 ? 128 : kP;
@@ -342,7 +408,8 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   const int half = gpr;    // group-interleaved table: second chunks start here
   const int mod_rows = p.batches * p.variants;
   float *scale_tab = reinterpret_cast<float *>(smem);
-  uint4 *w_s = smem + kScaleTab / 4;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kScaleTab / 4);
+  uint4 *w_s = smem + kHeadUint4;
   uint4 *m1_s = w_s + (kTables ? kc : 0);
   uint4 *sh_s = m1_s + (kTables ? kc * mod_rows : 0);
   uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + wid * 2 * row_chunks;
@@ -390,7 +457,49 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
       }
     }
   }
+  // TMEM columns of lane l: w of its groups i = 0 .. gpl-1 at 8 i, then bf16(1 + scale) of table row t at
+  // 8 gpl (1 + t) + 8 i, then shift row t at 8 gpl (1 + mod_rows + t) + 8 i
+  constexpr int kGpl = kK ? (kK / 16 + 31) / 32 : 1;  // groups per lane
+  uint32_t tlane = 0;
+  if constexpr (kTmem) {
+    __syncwarp();
+    if (wid == 0) tmem_alloc(tmem_slot);
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
+    tlane = *tmem_slot + (uint32_t(32 * (wid & 3)) << 16);
+    {  // the kWarps / 4 warps of each lane quarter share the writes of that quarter's copy
+      constexpr int kWriters = kWarps / 4;
+#pragma unroll
+      for (int i = 0; i < kGpl; ++i) {
+        if (i % kWriters != (wid >> 2) % kWriters) continue;
+        const int g = lane + 32 * i;
+        uint32_t v[8];
+        unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), v);
+        tmem_st8(tlane + 8 * i, v);
+        for (int t = 0; t < mod_rows; ++t) {
+          const int bt = t / p.variants;
+          const bool noisy = (t % p.variants) == 0;
+          const __nv_bfloat16 *mrow = (noisy ? p.noisy : p.clean) + bt * p.mod_stride;
+          load_mod8(mrow, int64_t(g) * 16, p.mods_vec, v);
+          load_mod8(mrow, int64_t(g) * 16 + 8, p.mods_vec, v + 4);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[k] = badd2(kOne2, v[k]);
+          tmem_st8(tlane + 8 * kGpl * (1 + t) + 8 * i, v);
+          if (kShift) {
+            const __nv_bfloat16 *srow = (noisy ? p.shift : p.shift_clean) + bt * p.mod_stride;
+            load_mod8(srow, int64_t(g) * 16, p.mods_vec, v);
+            load_mod8(srow, int64_t(g) * 16 + 8, p.mods_vec, v + 4);
+            tmem_st8(tlane + 8 * kGpl * (1 + mod_rows + t) + 8 * i, v);
+          }
+        }
+      }
+      tmem_wait_st();
+    }
+    tmem_fence_before_sync();
+  }
   __syncthreads();  // scale table (and constant tables) visible to every warp
+  if constexpr (kTmem) tmem_fence_after_sync();
 
   // row m = b * S + s; b, s and b % batches advance by fixed steps instead of dividing per row
   const int S = int(p.S);
@@ -480,10 +589,17 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     // scale-byte offset = row part + group part (fibo/fp4.py:60)
     const int64_t sf_row = (m >> 7) * (K / 64 * 512) + (m & 31) * 16 + ((m & 127) >> 5) * 4;
 
-    auto group = [&](int g, int xi) {  // xi: chunk index of x chunk 2g in the row buffer
+    auto group = [&](int g, int xi, int i) {  // xi: chunk index of x chunk 2g in the row buffer; g = lane + 32 i
       uint32_t xu[8], wu[8], mv[8], sv[8];
       unpack16(row_s[xi], row_s[xi ^ 1], xu);
-      if (kTables) {
+      if constexpr (kTmem) {
+        const uint32_t aw = tlane + 8 * i, am = tlane + 8 * kGpl * (1 + t) + 8 * i;
+        if (kShift) {
+          tmem_ld8x3(aw, am, tlane + 8 * kGpl * (1 + mod_rows + t) + 8 * i, wu, mv, sv);
+        } else {
+          tmem_ld8x2(aw, am, wu, mv);
+        }
+      } else if (kTables) {
         unpack16(w_s[g], w_s[half + g], wu);
         unpack16(m1_row[g], m1_row[half + g], mv);
         if (kShift) unpack16(sh_row_s[g], sh_row_s[half + g], sv);
@@ -520,19 +636,20 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
       }
     };
     if (kK) {
+      if (kTmem) __syncwarp();  // tcgen05.ld is warp-collective
       // g = lane + 32 i: chunk 2g is at x_lane + 64 i with the swizzle key's bits 2-3 advanced by i
 #pragma unroll
       for (int i = 0; i < (kK / 16 + 31) / 32; ++i) {
         const int g = lane + 32 * i;
-        if ((kK / 16) % 32 == 0 || g < gpr) group(g, (x_lane + 64 * i) ^ (4 * (i & 3)));
+        if ((kK / 16) % 32 == 0 || g < gpr) group(g, (x_lane + 64 * i) ^ (4 * (i & 3)), i);
       }
     } else {
       int g = lane;
       for (; g + 32 < gpr; g += 64) {  // two independent groups per iteration
-        group(g, swz(2 * g));
-        group(g + 32, swz(2 * g + 64));
+        group(g, swz(2 * g), 0);
+        group(g + 32, swz(2 * g + 64), 0);
       }
-      if (g < gpr) group(g, swz(2 * g));
+      if (g < gpr) group(g, swz(2 * g), 0);
     }
     __syncwarp();  // every lane is done with this buffer before it is refilled
   }
@@ -544,11 +661,19 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
     if (lane == 0) atomicMax(reinterpret_cast<unsigned int *>(p.amax), __float_as_uint(v));  // v >= 0
   }
+  if constexpr (kTmem) {  // every warp's TMEM reads are complete before the columns are released
+    tmem_fence_before_sync();
+    __syncthreads();
+    if (wid == 0) {
+      tmem_fence_after_sync();
+      tmem_dealloc(*tmem_slot);
+    }
+  }
 }
 
-template <int kK, int kWarps, bool kTables, bool kShift, bool kAmax>
+template <int kK, int kWarps, int kTab, bool kShift, bool kAmax>
 int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
-  auto kernel = norm_scale_fp4_kernel<kK, kWarps, kTables, kShift, kAmax>;
+  auto kernel = norm_scale_fp4_kernel<kK, kWarps, kTab, kShift, kAmax>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -560,37 +685,54 @@ int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kWarps * 32, smem) != cudaSuccess || occ < 1)
     occ = 1;
+  // TMEM tables: at most two CTAs per SM, so their allocations always fit the SM's 512 columns
+  if (kTab == 2 && occ > int(512 / kTmemCols)) occ = int(512 / kTmemCols);
   const int64_t blocks_needed = (p.padded + kWarps - 1) / kWarps;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(blocks_needed, int64_t(sm_count()) * occ));
   kernel<<<dim3(unsigned(blocks)), dim3(kWarps * 32), smem, stream>>>(p);
   return cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
 }
 
-template <int kK, bool kTables, bool kShift, bool kAmax>
+template <int kK, int kTab, bool kShift, bool kAmax>
 int launch_norm_warps(int warps, const NormParams &p, size_t smem, cudaStream_t stream) {
-  switch (warps) {
-    case 16: return launch_norm_typed<kK, 16, kTables, kShift, kAmax>(p, smem, stream);
-    case 8: return launch_norm_typed<kK, 8, kTables, kShift, kAmax>(p, smem, stream);
-    case 6: return launch_norm_typed<kK, 6, kTables, kShift, kAmax>(p, smem, stream);
-    case 4: return launch_norm_typed<kK, 4, kTables, kShift, kAmax>(p, smem, stream);
-    default: return launch_norm_typed<kK, 2, kTables, kShift, kAmax>(p, smem, stream);
+  if constexpr (kTab == 2) {  // 16 or 8 warps: one CTA per SM
+    if (warps == 16) return launch_norm_typed<kK, 16, kTab, kShift, kAmax>(p, smem, stream);
+    return launch_norm_typed<kK, 8, kTab, kShift, kAmax>(p, smem, stream);
+  } else {
+    switch (warps) {
+      case 16: return launch_norm_typed<kK, 16, kTab, kShift, kAmax>(p, smem, stream);
+      case 8: return launch_norm_typed<kK, 8, kTab, kShift, kAmax>(p, smem, stream);
+      case 6: return launch_norm_typed<kK, 6, kTab, kShift, kAmax>(p, smem, stream);
+      case 4: return launch_norm_typed<kK, 4, kTab, kShift, kAmax>(p, smem, stream);
+      default: return launch_norm_typed<kK, 2, kTab, kShift, kAmax>(p, smem, stream);
+    }
   }
 }
 
 template <int kK, bool kAmax>
-int launch_norm_k(bool tables, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
-  return tables ? (shift ? launch_norm_warps<kK, true, true, kAmax>(warps, p, smem, st)
-                         : launch_norm_warps<kK, true, false, kAmax>(warps, p, smem, st))
-                : (shift ? launch_norm_warps<kK, false, true, kAmax>(warps, p, smem, st)
-                         : launch_norm_warps<kK, false, false, kAmax>(warps, p, smem, st));
+int launch_norm_k(int tab, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
+  if constexpr (kK != 0) {
+    if (tab == 2)
+      return shift ? launch_norm_warps<kK, 2, true, kAmax>(warps, p, smem, st)
+                   : launch_norm_warps<kK, 2, false, kAmax>(warps, p, smem, st);
+  }
+  return tab == 1 ? (shift ? launch_norm_warps<kK, 1, true, kAmax>(warps, p, smem, st)
+                           : launch_norm_warps<kK, 1, false, kAmax>(warps, p, smem, st))
+                  : (shift ? launch_norm_warps<kK, 0, true, kAmax>(warps, p, smem, st)
+                           : launch_norm_warps<kK, 0, false, kAmax>(warps, p, smem, st));
 }
+
+// 0: per-column constants in TMEM where eligible (default); 1: never TMEM (shared-memory / global tables)
+std::atomic<int> g_norm_table_mode{0};
+bool tmem_tables_enabled() { return g_norm_table_mode.load(std::memory_order_relaxed) == 0; }
 
 // Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
 // multiple of 64 takes the runtime-K kernel.
+constexpr int64_t kFixedK = 3072;
 template <bool kAmax>
-int launch_norm(bool tables, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
-  if (p.K == 3072) return launch_norm_k<3072, kAmax>(tables, shift, warps, p, smem, st);
-  return launch_norm_k<0, kAmax>(tables, shift, warps, p, smem, st);
+int launch_norm(int tab, bool shift, int warps, const NormParams &p, size_t smem, cudaStream_t st) {
+  if (p.K == kFixedK) return launch_norm_k<kFixedK, kAmax>(tab, shift, warps, p, smem, st);
+  return launch_norm_k<0, kAmax>(tab, shift, warps, p, smem, st);
 }
 
 // ---- SiLU(gate) * value -> NVFP4 ---------------------------------------------------------------
@@ -779,12 +921,18 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   const bool has_shift = shift != nullptr;
   const size_t row_pair = 2 * size_t(p.row_chunks) * 16;
   constexpr size_t kSmemMax = 227 * 1024;
+  constexpr size_t kHead = qe::kHeadUint4 * 16;
   const size_t tables = qe::norm_table_bytes(K, int64_t(p.batches) * p.variants, has_shift);
-  const bool use_tables = tables <= 64 * 1024;
+  // per-column constants: TMEM when K is the specialised width and they fit the allocation, else shared-memory
+  // tables up to 64 KiB, else global memory
+  const int64_t tmem_cols = 8 * ((K / 16 + 31) / 32) * (1 + int64_t(p.batches) * p.variants * (has_shift ? 2 : 1));
+  int tab = tables <= 64 * 1024 ? 1 : 0;
+  if (K == qe::kFixedK && tmem_cols <= int64_t(qe::kTmemCols) && qe::tmem_tables_enabled()) tab = 2;
   int best_warps = 0, best_resident = 0;
   size_t best_smem = 0;
   for (int w : {16, 8, 6, 4, 2}) {
-    const size_t smem = qe::kScaleTab * sizeof(float) + size_t(w) * row_pair + (use_tables ? tables : 0);
+    if (tab == 2 && w < 8) continue;
+    const size_t smem = kHead + size_t(w) * row_pair + (tab == 1 ? tables : 0);
     if (smem > kSmemMax) continue;
     const int per_sm = std::min<int>(int(kSmemMax / smem), 32 / w);
     if (per_sm * w > best_resident) {
@@ -795,8 +943,8 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   }
   if (best_warps == 0) return fail(QE_ERR_INVALID, "qe_norm_scale_fp4: K too large for two rows per warp");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return amax ? qe::launch_norm<true>(use_tables, has_shift, best_warps, p, best_smem, st)
-              : qe::launch_norm<false>(use_tables, has_shift, best_warps, p, best_smem, st);
+  return amax ? qe::launch_norm<true>(tab, has_shift, best_warps, p, best_smem, st)
+              : qe::launch_norm<false>(tab, has_shift, best_warps, p, best_smem, st);
 }
 }  // namespace
 }  // namespace qe
@@ -818,6 +966,12 @@ int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const vo
   int s = qe::norm_scale_impl(x, w, noisy, clean, mask, shift, shift_clean, nullptr, M, S, K, mod_stride, eps,
                               nullptr, nullptr, amax, stream);
   return s ? s : qe::ok();
+}
+
+int qe_set_norm_table_mode(int32_t mode) {
+  if (mode < 0 || mode > 1) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0 or 1");
+  qe::g_norm_table_mode.store(mode, std::memory_order_relaxed);
+  return qe::ok();
 }
 
 int qe_silu_table_init(uint16_t *table, void *stream) {

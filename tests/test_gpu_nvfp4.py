@@ -75,18 +75,37 @@ def _norm_case(B, S, K, eps, masked, shift, seed, x_scale=1.0):
     return out, q_ref, sf_ref
 
 
+@pytest.fixture(params=[0, 1], ids=["tmem_tables", "smem_tables"])
+def table_mode(request):
+    """Both homes of the per-column constants (tensor memory where eligible, or shared memory)."""
+    from qwenedit_b200 import _lib
+    _lib.call("qe_set_norm_table_mode", request.param)
+    yield request.param
+    _lib.call("qe_set_norm_table_mode", 0)
+
+
 @pytest.mark.parametrize("T", [4096, 16384])
 @pytest.mark.parametrize("shift", [False, True])
-def test_norm_scale_baseline_shapes(T, shift):
+def test_norm_scale_baseline_shapes(T, shift, table_mode):
     """BASELINE NVFP4: x [1, T, 3072] ~N(0,1), eps 1e-6, w ~ 1 + 0.02 N, scale/shift ~ 0.1 N."""
     out, q_ref, sf_ref = _norm_case(1, T, 3072, 1e-6, False, shift, seed=T + shift)
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
 
-@pytest.mark.parametrize("K", [64, 128, 192, 1024, 3584, 4096, 4160, 8192, 12288])
+@pytest.mark.parametrize("K", [64, 128, 192, 1024, 3072, 3584, 4096, 4160, 8192, 12288])
 def test_norm_scale_widths_masks_batches(K):
     out, q_ref, sf_ref = _norm_case(3, 67, K, 1e-5, True, K % 3 == 0, seed=K, x_scale=3.0)
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@pytest.mark.parametrize("B,masked,shift", [(1, True, True), (2, True, False), (2, False, True), (4, False, False),
+                                            (3, False, True), (5, False, False)])
+def test_norm_scale_k3072_table_layouts(B, masked, shift, table_mode):
+    """K = 3072 with 1-5 modulation rows (x2 with a mask, x2 with a shift): the specialised kernel with its
+    constants in tensor memory (up to 256 columns) or in shared memory, bit-exact either way."""
+    out, q_ref, sf_ref = _norm_case(B, 300, 3072, 1e-6, masked, shift, seed=B * 10 + masked * 2 + shift)
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
