@@ -413,7 +413,9 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   uint4 *m1_s = w_s + (kTables ? kc : 0);
   uint4 *sh_s = m1_s + (kTables ? kc * mod_rows : 0);
   uint4 *bufs = sh_s + (kTables && kShift ? kc * mod_rows : 0) + wid * 2 * row_chunks;
-  const int64_t warp0 = int64_t(blockIdx.x) * kWarps + wid;
+  // warps are numbered CTA-minor, so consecutive rows go to different SMs and every SM gets the same number of
+  // rows (to within one per warp slot) whatever M is
+  const int64_t warp0 = int64_t(wid) * gridDim.x + blockIdx.x;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
   const float kf = float(K);
@@ -788,7 +790,7 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
   const int gpr = int(p.K >> 4);
   const int segs = (gpr + 31) >> 5;
   const int64_t items = p.M * segs;
-  const int64_t warp = (int64_t(blockIdx.x) * kSiluThreads + threadIdx.x) >> 5;
+  const int64_t warp = int64_t(threadIdx.x >> 5) * gridDim.x + blockIdx.x;  // CTA-minor: items spread over SMs
   const int64_t nwarps = (int64_t(gridDim.x) * kSiluThreads) >> 5;
   uint32_t amax_w = 0u;  // kAmax: running bf16x2 max of |y|
 
