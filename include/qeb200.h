@@ -158,6 +158,32 @@ int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const vo
 int qe_silu_mul_amax(const void *gate, const void *value, int64_t M, int64_t K, const uint16_t *silu_table,
                      float *amax, void *stream);
 
+/* ---- head-sharded pools across the GPUs of one node ------------------------------------------
+ *
+ * No counterpart in the reference, which keeps a prefix on one GPU and disables the pool under tensor or
+ * sequence parallelism (multi_turn/pipeline/encoding.py:214-220). Rank r of an n-GPU group owns heads
+ * [r H/n, (r+1) H/n) of every pooled token; every rank runs the same index decisions, so slots agree.
+ */
+
+/* CUDA IPC plumbing: qe_ipc_alloc makes a `bytes` device allocation on the current device and writes its
+ * 64-byte cudaIpcMemHandle to `handle`; qe_ipc_open maps a handle made by another process into this one (peer
+ * access enabled on first use); qe_ipc_close / qe_ipc_free undo them. */
+int qe_ipc_alloc(int64_t bytes, void **ptr, uint8_t *handle);
+int qe_ipc_free(void *ptr);
+int qe_ipc_open(const uint8_t *handle, void **ptr);
+int qe_ipc_close(void *ptr);
+
+/* Append with the head scatter fused in: `src` holds n_tokens rows of all heads (n_peers * slice_bytes bytes
+ * per plane row, planes as for the copies above); slice r of the row of token t is written to row slots[t] of
+ * plane p of rank r's pool, whose base is peer_pools[r] (a host array of n_peers device pointers, this rank's
+ * own pool at its rank; mapped peer pools from qe_ipc_open). `pool` gives the plane strides shared by every
+ * rank's pool (its base is ignored); its rows are slice_bytes long. Slots outside [0, pool_rows) are skipped
+ * and set *err_flag. The peer writes are visible to the other ranks after a stream-ordered barrier that follows
+ * this launch on `stream` (for example an NCCL all-reduce). n_peers <= 8. */
+int qe_append_scatter(const void *const *peer_pools, int32_t n_peers, qe_planes pool, int64_t pool_rows,
+                      qe_planes src, int32_t n_planes, int64_t slice_bytes, const int64_t *slots, int64_t n_tokens,
+                      int32_t *err_flag, void *stream);
+
 /* ---- prefix index: radix tree + slot allocator + LRU eviction (host) -------------------------
  *
  * Restates the behaviour of SGLang's RadixCache (page_size 1 and paged) and TokenToKVPoolAllocator

@@ -48,6 +48,12 @@ SIGNATURES: dict[str, list] = {
                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
     "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "qe_silu_table_init": [c_void_p, c_void_p],
+    "qe_ipc_alloc": [c_int64, POINTER(c_void_p), c_void_p],
+    "qe_ipc_free": [c_void_p],
+    "qe_ipc_open": [c_void_p, POINTER(c_void_p)],
+    "qe_ipc_close": [c_void_p],
+    "qe_append_scatter": [c_void_p, c_int32, Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int64,
+                          c_void_p, c_void_p],
     "qe_set_norm_table_mode": [c_int32],
     "qe_norm_scale_amax": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p],

@@ -164,26 +164,40 @@ def cat_slots(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def pool_geometry(layers, heads, head_dim, budget_bytes, dtype, extra_dim=0, page_size=1) -> tuple[int, int, int]:
+    """(capacity tokens, rows, bytes per token) of a pool: capacity = budget // bytes per token rounded down to
+    whole pages (paged.py:44-47), plus one padding page of rows."""
+    if page_size < 1:
+        raise ValueError("page_size must be >= 1")
+    elem = torch.empty((), dtype=dtype).element_size()
+    per_token = layers * 2 * heads * head_dim * elem + extra_dim * elem
+    capacity = max(int(budget_bytes // per_token), 1)
+    capacity = max(capacity // page_size, 1) * page_size
+    return capacity, capacity + page_size, per_token
+
+
 class PagedKVPool:
     """Paged K/V prefix pool on one GPU (paged.py:40-131)."""
 
-    def __init__(self, name, layers, heads, head_dim, budget_bytes, dtype, device, extra_dim=0, page_size=1):
-        elem = torch.empty((), dtype=dtype).element_size()
-        per_token = layers * 2 * heads * head_dim * elem + extra_dim * elem
-        if page_size < 1:
-            raise ValueError("page_size must be >= 1")
+    def __init__(self, name, layers, heads, head_dim, budget_bytes, dtype, device, extra_dim=0, page_size=1,
+                 kv=None):
+        """`kv` (an addition): storage for the [L, 2, rows, H, D] pool allocated by the caller (the head-sharded
+        pools pass memory that other processes can map); by default the pool allocates it."""
+        self.capacity, self.rows, per_token = pool_geometry(layers, heads, head_dim, budget_bytes, dtype, extra_dim,
+                                                            page_size)
         self.name = name
         self.page_size = int(page_size)
-        capacity = max(int(budget_bytes // per_token), 1)
-        pages = max(capacity // self.page_size, 1)
-        self.capacity = pages * self.page_size
         self.layers, self.heads, self.head_dim = layers, heads, head_dim
         self.extra_dim = extra_dim
-        self.rows = self.capacity + self.page_size  # row 0 (page 0) is the allocator's padding
         self.device = torch.device(device)
         if self.device.type == "cuda" and self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
-        self.kv = torch.empty(layers, 2, self.rows, heads, head_dim, dtype=dtype, device=self.device)
+        shape = (layers, 2, self.rows, heads, head_dim)
+        if kv is None:
+            kv = torch.empty(shape, dtype=dtype, device=self.device)
+        elif tuple(kv.shape) != shape or kv.dtype != dtype or kv.device != self.device or not kv.is_contiguous():
+            raise ValueError(f"kv storage must be a contiguous {list(shape)} {dtype} tensor on {self.device}")
+        self.kv = kv
         self.extra = (
             torch.empty(self.rows, extra_dim, dtype=dtype, device=self.device) if extra_dim else None
         )
