@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
-    ap.add_argument("--workload", choices=["edit_1k", "serving"], default="edit_1k",
+    ap.add_argument("--workload", choices=["edit_1k", "serving", "headshard"], default="edit_1k",
                     help="edit_1k: the 1K-edit turn (default, the headline); serving: 64 mixed 1K/2K sessions")
     ap.add_argument("--profile", choices=["gather", "append", "norm", "silu"], default=None,
                     help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
@@ -688,6 +688,102 @@ def run_serving(args, rank, world, local):
         }), flush=True)
 
 
+# ---- one 2K session head-sharded over all ranks (strong scaling) ---------------------------------------
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this node type
+
+
+def run_headshard(args, rank, world, local):
+    """One 2K edit session whose pool is split by head over the ranks (HeadShardedKVPool): every denoising
+    step each rank gathers its heads of the 16,896-token prefix locally; once per turn the 16,384 new image
+    tokens, held sequence-parallel (rank r has tokens [r T/n, (r+1) T/n) with all heads), are appended with
+    the fused head-scatter kernel over NVLink, followed by the stream-ordered barrier."""
+    from qwenedit_b200.sharded import HeadShardedKVPool
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    img = IMAGE_TOKENS["2k"]
+    prefix = TEXT + img
+    pool = HeadShardedKVPool("dit-2k", L, H, D, POOL_GIB << 30, torch.bfloat16, device, page_size=PAGE)
+    pool.pool.index.shuffle_free(5)  # same seed on every rank: the index is replicated
+    hl = pool.heads_local
+    rng = np.random.default_rng(9)  # the session's ids: the same on every rank
+    text = rng.integers(1, 1 << 62, size=TEXT)
+    images = [rng.integers(1, 1 << 62, size=img) for _ in range(args.steps + args.warmup + 2)]
+    lo, hi = rank * img // world, (rank + 1) * img // world
+    new_kv = torch.empty(L, 2, hi - lo, H, D, dtype=torch.bfloat16, device=device)
+    new_kv.normal_()
+    out = torch.empty(L, 2, prefix, hl, D, dtype=torch.bfloat16, device=device)
+    first = pool.alloc(prefix)  # turn 0's prefix, computed on a miss: every rank writes its heads
+    pool.write(first, torch.randn(L, 2, prefix, hl, D, dtype=torch.bfloat16, device=device))
+    pool.insert(np.concatenate([text, images[0]]), first, owned_from=0)
+    stream = torch.cuda.current_stream(device)
+
+    def turn(t, ev=None):
+        m = pool.match(np.concatenate([text, images[t]]))
+        if m.length != prefix:
+            raise RuntimeError(f"turn {t}: expected a full prefix hit, got {m.length}")
+        for _ in range(STEPS_PER_TURN):
+            pool.gather_into(m.indices, out)
+        slots = pool.alloc(img)
+        if slots is None:
+            raise RuntimeError("pool exhausted")
+        if ev is not None:
+            ev[0].record(stream)
+        pool.write_scatter(slots[lo:hi], new_kv)
+        if ev is not None:
+            ev[1].record(stream)
+        pool.barrier()
+        idx_host = np.concatenate([m.indices._qe_host[:TEXT], slots._qe_host])
+        idx = torch.from_numpy(idx_host)
+        idx._qe_host = idx_host
+        pool.insert(np.concatenate([text, images[t + 1]]), idx, owned_from=TEXT)
+        m.release()
+
+    for t in range(args.warmup):
+        turn(t)
+    pool.verify_replicas()
+    scatter_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        turn(args.warmup + i, scatter_ev[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    elapsed = max_over_ranks(t0.elapsed_time(t1), world, device)
+    scatter_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in scatter_ev), world, device)
+    if pool.device_errors():
+        raise RuntimeError("a paged copy kernel reported an error")
+    pool.verify_replicas()
+    gather_bytes = 2 * L * 2 * prefix * ROW  # all heads, summed over the ranks
+    append_bytes = 2 * L * 2 * img * ROW
+    turn_bytes = STEPS_PER_TURN * gather_bytes + append_bytes
+    nvlink_per_rank = (world - 1) * L * 2 * (hi - lo) * hl * D * 2
+    if rank == 0:
+        peak, _ = measured_peak()
+        value = turn_bytes / (elapsed / args.steps) / 1e6
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen_image_2.1_2k_edit_head_sharded", "layers": L, "heads": H, "head_dim": D,
+                       "heads_per_gpu": hl, "prefix_tokens": prefix, "append_tokens": img, "page_tokens": PAGE,
+                       "gathers_per_turn": STEPS_PER_TURN, "pool_gib_per_gpu": POOL_GIB,
+                       "append": "sequence-parallel rows scattered to head owners (qe_append_scatter)"},
+            "frac_of_measured_hbm_per_gpu": round(value / world / peak, 4),
+            "dit_step_ms_2k": round((elapsed / args.steps - scatter_ms) / STEPS_PER_TURN, 4),
+            "scatter": {"ms": round(scatter_ms, 4), "nvlink_bytes_per_gpu": nvlink_per_rank,
+                        "nvlink_GB/s_per_gpu": round(nvlink_per_rank / scatter_ms / 1e6, 1) if world > 1 else None,
+                        "frac_of_nvlink": round(nvlink_per_rank / scatter_ms / 1e6 / NVLINK_GBS, 4)
+                        if world > 1 else None},
+            "gpu_launches": args.steps * (STEPS_PER_TURN + 1),
+        }), flush=True)
+    pool.close()
+
+
 def profile_case(kind: str) -> None:
     """A small case of one kernel for ncu captures: inputs > L2, a few GB on the device, 6 launches."""
     from types import SimpleNamespace
@@ -755,8 +851,8 @@ def main():
         }), flush=True)
         return
 
-    if args.workload == "serving":
-        run_serving(args, rank, world, local)
+    if args.workload in ("serving", "headshard"):
+        (run_serving if args.workload == "serving" else run_headshard)(args, rank, world, local)
         if world > 1:
             torch.distributed.destroy_process_group()
         return
