@@ -239,3 +239,38 @@ def test_amax_edge_cases():
     first = silu_mul_amax(g, v).item()
     assert first == y.float().abs().max().item() and first > 1e5
     assert silu_mul_amax(g[:, :500], v[:, :500]).item() == y[:, :500].float().abs().max().item()
+
+
+def test_wrappers_replay_in_a_cuda_graph(table_mode):
+    """norm_scale_fp4, silu_mul_fp4 and the amax pre-pass captured in one CUDA graph: a replay on new inputs
+    (written in place) gives the same bytes as eager calls on those inputs."""
+    K, T = 3072, 640
+    x = inputs.bf16(301, (1, T, K)).to(DEV)
+    norm = SimpleNamespace(weight=inputs.bf16(302, (K,), scale=0.02, shift=1.0).to(DEV), eps=1e-6)
+    mods = inputs.bf16(303, (1, 4 * K), scale=0.1).to(DEV)
+    noisy, clean = mods[:, :K], mods[:, K:2 * K]
+    mask = torch.from_numpy(inputs.uniforms(304, T) < 0.5).to(DEV)
+    g = inputs.bf16(305, (T, 2 * K)).to(DEV)
+    v = inputs.bf16(306, (T, 2 * K)).to(DEV)
+    gs = _gs(40.0)
+
+    def work():
+        return (norm_scale_fp4(x, norm, noisy, clean, mask, gs), silu_mul_fp4(g, v, gs), silu_mul_amax(g, v))
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            work()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = work()
+    x.copy_(inputs.bf16(311, (1, T, K)).to(DEV))
+    g.copy_(inputs.bf16(312, (T, 2 * K)).to(DEV))
+    graph.replay()
+    torch.cuda.synchronize()
+    eager = work()
+    for a, b in ((captured[0].q, eager[0].q), (captured[0].sf, eager[0].sf), (captured[1].q, eager[1].q),
+                 (captured[1].sf, eager[1].sf), (captured[2], eager[2])):
+        assert torch.equal(a, b)
