@@ -392,7 +392,48 @@ def extras(pool, sess, device):
     torch.cuda.empty_cache()
     out.update(nvfp4_extras(device, peak))
     out["nvfp4_cpu_baseline"] = nvfp4_cpu()
+    out["mask_blend_1k"] = latent_extras(device)
     return out
+
+
+def latent_extras(device):
+    """Per-step mask blend on 1K latents [1, 4096, 64] bf16, one launch (the reference's eager blend is about ten
+    launches): device time per call from a CUDA graph of 100 calls (no host time in it), and the host time of an
+    eager call."""
+    from qwenedit_b200.latents import mask_blend
+
+    lat = torch.randn(1, 4096, 64, device=device).bfloat16()
+    x0, eps = torch.randn_like(lat), torch.randn_like(lat)
+    m = torch.rand(1, 4096, 1, device=device)
+    sigma = torch.tensor(0.5, device=device)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(5):
+            mask_blend(lat, x0, eps, m, sigma)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(100):
+            mask_blend(lat, x0, eps, m, sigma)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    device_us = a.elapsed_time(b) / 100 * 1e3
+    t0 = time.perf_counter()
+    for _ in range(200):
+        mask_blend(lat, x0, eps, m, sigma)
+    host_us = (time.perf_counter() - t0) / 200 * 1e6
+    torch.cuda.synchronize()
+    del graph
+    nbytes = 4 * lat.numel() * 2 + m.numel() * 4
+    return {"device_us_per_call": round(device_us, 2), "host_us_per_call": round(host_us, 1),
+            "launches_per_call": 1, "bytes_per_call": nbytes,
+            "GB/s": round(nbytes / device_us / 1e3, 1)}
 
 
 def _time_kernel(fn, flush, iters=20):

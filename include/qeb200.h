@@ -184,6 +184,31 @@ int qe_append_scatter(const void *const *peer_pools, int32_t n_peers, qe_planes 
                       qe_planes src, int32_t n_planes, int64_t slice_bytes, const int64_t *slots, int64_t n_tokens,
                       int32_t *err_flag, void *stream);
 
+/* ---- per-step latent ops (device) -----------------------------------------------------------
+ *
+ * dtype codes: 0 = fp32, 1 = bf16, 2 = fp16.
+ */
+
+/* MaskState.blend (multi_turn/pipeline/masking.py:82-89) in one launch:
+ *   s = sigma.to(dtype); keep = (1 - s) x0 + s eps; out = m lat + (1 - m) keep,   m = mask.to(dtype)
+ * with torch's eager rounding: each op in fp32, rounded to `dtype`. latents / out [B, N, C] contiguous in
+ * `dtype`; x0 / eps [*, N, C] in `dtype` with x0_bstride / eps_bstride elements between batch entries (0 =
+ * broadcast); mask [*, N, mask_channels] (1 or C) in mask_dtype with mask_bstride; sigma one value of
+ * sigma_dtype on the device, or sigma_dtype 3: two fp32 values {s, 1 - s} kept unrounded (a Python-float sigma). */
+int qe_mask_blend(const void *latents, const void *x0, const void *eps, const void *mask, const void *sigma,
+                  void *out, int64_t B, int64_t N, int64_t C, int64_t x0_bstride, int64_t eps_bstride,
+                  int64_t mask_bstride, int32_t mask_channels, int32_t dtype, int32_t mask_dtype, int32_t sigma_dtype,
+                  void *stream);
+
+/* _compose (multi_turn/pipeline/hooks.py:234-247) in one launch: out [h, w] cells = base, except the box
+ * [y0, y1) x [x0, x1) taken from crop [(y1 - y0), (x1 - x0)] cells; a cell is row_bytes bytes (C latent values). */
+int qe_latent_compose(const void *base, const void *crop, void *out, int64_t h, int64_t w, int64_t row_bytes,
+                      int64_t x0, int64_t y0, int64_t x1, int64_t y1, void *stream);
+
+/* stored_latents with a crop box (multi_turn/state.py:52-62): out = src cells of the box, row-major. */
+int qe_latent_crop(const void *src, void *out, int64_t h, int64_t w, int64_t row_bytes, int64_t x0, int64_t y0,
+                   int64_t x1, int64_t y1, void *stream);
+
 /* ---- prefix index: radix tree + slot allocator + LRU eviction (host) -------------------------
  *
  * Restates the behaviour of SGLang's RadixCache (page_size 1 and paged) and TokenToKVPoolAllocator

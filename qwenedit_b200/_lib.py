@@ -48,6 +48,11 @@ SIGNATURES: dict[str, list] = {
                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p],
     "qe_silu_mul_fp4": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "qe_silu_table_init": [c_void_p, c_void_p],
+    "qe_mask_blend": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                      c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p],
+    "qe_latent_compose": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+                          c_int64, c_void_p],
+    "qe_latent_crop": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p],
     "qe_ipc_alloc": [c_int64, POINTER(c_void_p), c_void_p],
     "qe_ipc_free": [c_void_p],
     "qe_ipc_open": [c_void_p, POINTER(c_void_p)],

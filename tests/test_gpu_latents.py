@@ -1,0 +1,63 @@
+"""Per-step latent kernels on the GPU, bit-exact against the reference's eager torch ops (oracle/latents_ref.py):
+the mask blend in bf16 / fp16 / fp32 with broadcast x0 and mask, fp32 or latent-dtype masks, tensor and Python
+float sigmas (including 0 and 1); compose and crop for boxes at the edges and inside the grid."""
+
+import pytest
+import torch
+
+from oracle import latents_ref
+from qwenedit_b200 import latents
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _case(B, N, C, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    lat = torch.randn(B, N, C, generator=g).to(dtype)
+    x0 = torch.randn(1, N, C, generator=g).to(dtype)
+    eps = torch.randn(B, N, C, generator=g).to(dtype)
+    m = torch.rand(1, N, 1, generator=g)
+    m[:, : N // 4] = 0.0
+    m[:, N // 4 : N // 2] = 1.0  # hard zeros and ones next to the feathered edge
+    return [t.to(DEV) for t in (lat, x0, eps, m)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("sigma", [0.0, 0.37, 1.0, "py"])
+def test_mask_blend_matches_eager(dtype, B, sigma):
+    lat, x0, eps, m = _case(B, 4096, 64, dtype, seed=B * 10)
+    s = 0.6180339887 if sigma == "py" else torch.tensor(sigma, dtype=torch.float32, device=DEV)
+    want = latents_ref.blend(lat, x0, eps, m, s)
+    got = latents.mask_blend(lat, x0, eps, m, s)
+    assert got.dtype == want.dtype and got.shape == want.shape
+    assert torch.equal(got, want)
+
+
+def test_mask_blend_latent_dtype_mask_per_channel():
+    lat, x0, eps, _ = _case(2, 1024, 16, torch.bfloat16, seed=5)
+    g = torch.Generator().manual_seed(6)
+    m = torch.rand(2, 1024, 16, generator=g).bfloat16().to(DEV)
+    s = torch.tensor(0.25, dtype=torch.bfloat16, device=DEV)
+    assert torch.equal(latents.mask_blend(lat, x0, eps, m, s), latents_ref.blend(lat, x0, eps, m, s))
+
+
+@pytest.mark.parametrize("box", [(0, 0, 64, 64), (3, 5, 17, 40), (60, 0, 64, 1), (0, 63, 64, 64)])
+@pytest.mark.parametrize("C,dtype", [(64, torch.bfloat16), (16, torch.float32), (3, torch.float16)])
+def test_compose_and_crop_match_eager(box, C, dtype):
+    h = w = 64
+    g = torch.Generator().manual_seed(C)
+    base = torch.randn(1, h * w, C, generator=g).to(dtype).to(DEV)
+    x0, y0, x1, y1 = box
+    piece = torch.randn(1, (y1 - y0) * (x1 - x0), C, generator=g).to(DEV)  # fp32: converted to the base dtype
+    assert torch.equal(latents.compose(base, (h, w), piece, box), latents_ref.compose(base, (h, w), piece, box))
+    assert torch.equal(latents.crop(base, (h, w), box), latents_ref.crop(base, (h, w), box))
+
+
+def test_bad_boxes_raise():
+    base = torch.zeros(1, 16, 4, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        latents.crop(base, (4, 4), (0, 0, 5, 1))
+    with pytest.raises(ValueError):
+        latents.compose(base, (4, 4), torch.zeros(1, 1, 4, device=DEV), (2, 2, 2, 3))
