@@ -131,10 +131,16 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
                       int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream);
 
 /* Where qe_norm_scale_fp4 / qe_norm_scale_amax keep the per-column constants (process-wide): 0 = default
- * (tensor memory when K is the specialised width 3072 and they fit 256 TMEM columns, else shared memory or
- * global memory), 1 = never tensor memory. Results are identical either way. No counterpart in the reference;
+ * (tensor memory when K is the specialised width 3072, M >= 12288 rows and they fit 256 TMEM columns, else
+ * shared memory or global memory), 1 = never tensor memory. Results are identical either way. No counterpart in the reference;
  * for measurement and tests. */
 int qe_set_norm_table_mode(int32_t mode);
+
+/* Where qe_silu_mul_fp4 / qe_silu_mul_amax read the SiLU table from (process-wide): 0 = by size (default),
+ * 1 = staged in shared memory by every CTA, 2 = global memory through the L1 cache (by size: below 1,024
+ * rows). Results are identical.
+ * No counterpart in the reference; for measurement and tests. */
+int qe_set_silu_table_mode(int32_t mode);
 
 /* Fill `table` (65,536 uint16, 16-byte aligned device memory) with bf16(silu(g)) for every bf16 bit pattern g:
  * bf16(g / (1 + exp(-g))) exactly as the fused kernel's arithmetic rounds it (fibo/fp4.py:90). Build it once

@@ -727,6 +727,16 @@ int launch_norm_k(int tab, bool shift, int warps, const NormParams &p, size_t sm
 // 0: per-column constants in TMEM where eligible (default); 1: never TMEM (shared-memory / global tables)
 std::atomic<int> g_norm_table_mode{0};
 bool tmem_tables_enabled() { return g_norm_table_mode.load(std::memory_order_relaxed) == 0; }
+// Below this many rows the per-CTA TMEM setup (allocation, table writes, fences) costs more than the shared-
+// memory traffic it saves (K = 3072, device time: 20.3 vs 19.8 us at 8,192 rows, 31.1 vs 32.2 us at 16,384,
+// 52.3 vs 57.7 us at 32,768).
+constexpr int64_t kTmemMinRows = 12288;
+
+// SiLU table home: 0 = by size (default), 1 = shared memory, 2 = global memory through L1
+std::atomic<int> g_silu_table_mode{0};
+// by size: the L1 form below this many rows (no 128 KiB staging per CTA; device time 5.4 vs 8.1 us at one
+// row, equal at 1,024, slower from 4,096 rows: 54.6 vs 50.4 us, K = 12288)
+constexpr int64_t kSiluL1Rows = 1024;
 
 // Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
 // multiple of 64 takes the runtime-K kernel.
@@ -773,19 +783,25 @@ constexpr int kSiluItems = 2;       // warp items (32 groups each) in flight per
 __device__ __forceinline__ uint32_t silu_lookup(const uint16_t *tab, uint32_t w) {
   return uint32_t(tab[w & 0xffffu]) | (uint32_t(tab[w >> 16]) << 16);
 }
+__device__ __forceinline__ uint32_t silu_lookup_l1(const uint16_t *tab, uint32_t w) {
+  return uint32_t(__ldg(tab + (w & 0xffffu))) | (uint32_t(__ldg(tab + (w >> 16))) << 16);
+}
 
 // A warp item is 32 consecutive 16-value groups of one row, one group per lane; kSiluItems items per
 // iteration so every lane has 8 16-byte loads in flight before it computes. kAmax: the calibration pre-pass —
 // the same y, reduced to max |y| instead of quantised and stored.
-template <bool kAmax>
+// kL1: the SiLU table is read from global memory through the L1 cache instead of being staged in shared
+// memory (no 128 KiB copy per CTA before the first row; lookups of the values a row actually uses stay in L1).
+template <bool kAmax, bool kL1>
 __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
   extern __shared__ uint4 tab4[];
-  float *scale_tab = reinterpret_cast<float *>(tab4 + kSiluTable / 8);
-  for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
+  float *scale_tab = reinterpret_cast<float *>(tab4 + (kL1 ? 0 : kSiluTable / 8));
+  if (!kL1)
+    for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
   if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
   __syncthreads();
-  const uint16_t *tab = reinterpret_cast<const uint16_t *>(tab4);
+  const uint16_t *tab = kL1 ? reinterpret_cast<const uint16_t *>(p.table) : reinterpret_cast<const uint16_t *>(tab4);
   const int lane = threadIdx.x & 31;
   const int gpr = int(p.K >> 4);
   const int segs = (gpr + 31) >> 5;
@@ -819,7 +835,9 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
       unpack16(ga[u], gb[u], gw);
       unpack16(va[u], vb[u], vw);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = bmul2(silu_lookup(tab, gw[i]), vw[i]);  // bf16(silu(g) * v)
+      for (int i = 0; i < 8; ++i) {  // bf16(silu(g) * v)
+        y[i] = bmul2(kL1 ? silu_lookup_l1(tab, gw[i]) : silu_lookup(tab, gw[i]), vw[i]);
+      }
       if constexpr (kAmax) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax_w = bamax2(amax_w, y[i]);
@@ -929,7 +947,8 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   // tables up to 64 KiB, else global memory
   const int64_t tmem_cols = 8 * ((K / 16 + 31) / 32) * (1 + int64_t(p.batches) * p.variants * (has_shift ? 2 : 1));
   int tab = tables <= 64 * 1024 ? 1 : 0;
-  if (K == qe::kFixedK && tmem_cols <= int64_t(qe::kTmemCols) && qe::tmem_tables_enabled()) tab = 2;
+  if (K == qe::kFixedK && tmem_cols <= int64_t(qe::kTmemCols) && qe::tmem_tables_enabled() && M >= qe::kTmemMinRows)
+    tab = 2;
   int best_warps = 0, best_resident = 0;
   size_t best_smem = 0;
   for (int w : {16, 8, 6, 4, 2}) {
@@ -968,6 +987,12 @@ int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const vo
   int s = qe::norm_scale_impl(x, w, noisy, clean, mask, shift, shift_clean, nullptr, M, S, K, mod_stride, eps,
                               nullptr, nullptr, amax, stream);
   return s ? s : qe::ok();
+}
+
+int qe_set_silu_table_mode(int32_t mode) {
+  if (mode < 0 || mode > 2) return fail(QE_ERR_INVALID, "qe_set_silu_table_mode: mode must be 0, 1 or 2");
+  qe::g_silu_table_mode.store(mode, std::memory_order_relaxed);
+  return qe::ok();
 }
 
 int qe_set_norm_table_mode(int32_t mode) {
@@ -1018,15 +1043,19 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.M = M;
   p.K = K;
   p.padded = padded;
-  constexpr size_t smem = size_t(kSiluTable) * 2 + kScaleTab * sizeof(float);
-  static bool attr_set[2][64] = {};
+  const int mode = g_silu_table_mode.load(std::memory_order_relaxed);
+  const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
+  const size_t smem = (l1 ? 0 : size_t(kSiluTable) * 2) + kScaleTab * sizeof(float);
+  static bool attr_set[4][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  auto kernel = amax ? silu_mul_fp4_kernel<true> : silu_mul_fp4_kernel<false>;
-  if (!attr_set[amax ? 1 : 0][dev]) {
+  auto kernel = amax ? (l1 ? silu_mul_fp4_kernel<true, true> : silu_mul_fp4_kernel<true, false>)
+                     : (l1 ? silu_mul_fp4_kernel<false, true> : silu_mul_fp4_kernel<false, false>);
+  const int variant = (amax ? 2 : 0) + (l1 ? 1 : 0);
+  if (!attr_set[variant][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_fp4: smem attribute");
-    attr_set[amax ? 1 : 0][dev] = true;
+    attr_set[variant][dev] = true;
   }
   const int64_t items = M * ((K / 16 + 31) / 32);  // warp items: 32 groups of one row
   const int64_t warps_per_block = kSiluThreads / 32;

@@ -110,8 +110,17 @@ def test_norm_scale_k3072_table_layouts(B, masked, shift, table_mode):
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
 
+@pytest.fixture(params=[1, 2], ids=["smem_table", "l1_table"])
+def silu_mode(request):
+    """Both homes of the SiLU table (staged in shared memory, or read through L1)."""
+    from qwenedit_b200 import _lib
+    _lib.call("qe_set_silu_table_mode", request.param)
+    yield request.param
+    _lib.call("qe_set_silu_table_mode", 0)
+
+
 @pytest.mark.parametrize("M,K", [(4096, 12288), (300, 9536), (1, 64), (129, 640)])
-def test_silu_mul_shapes(M, K):
+def test_silu_mul_shapes(M, K, silu_mode):
     gate = inputs.bf16(M + K, (1, M, K))
     value = inputs.bf16(M + K + 1, (1, M, K))
     y = (torch.nn.functional.silu(gate.float()).bfloat16().float() * value.float()).bfloat16()
@@ -206,7 +215,7 @@ def test_norm_scale_amax_is_the_exact_max_of_y(B, S, K, masked, shift, shared):
 
 
 @pytest.mark.parametrize("M,K", [(4096, 12288), (300, 9536), (1, 64), (129, 640)])
-def test_silu_mul_amax_is_the_exact_max_of_y(M, K):
+def test_silu_mul_amax_is_the_exact_max_of_y(M, K, silu_mode):
     gate = inputs.bf16(M + K + 2, (1, M, K), scale=3.0)
     value = inputs.bf16(M + K + 3, (1, M, K))
     y = _oracle_silu_y(gate, value)
