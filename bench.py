@@ -393,7 +393,33 @@ def extras(pool, sess, device):
     out.update(nvfp4_extras(device, peak))
     out["nvfp4_cpu_baseline"] = nvfp4_cpu()
     out["mask_blend_1k"] = latent_extras(device)
+    out["encoder_prompt_1k"] = encoder_extras(device, peak)
     return out
+
+
+def encoder_extras(device, peak):
+    """Text-encoder pool (Qwen2.5-VL: 28 layers, 4 KV heads x 128, hidden 3584; 4 GiB, token-granular slots):
+    a full hit of a 1,024-token prompt returns the hidden rows (encoder.py:114), a partial hit gathers the
+    prefix K/V (encoder.py:173). Single launches between CUDA events after an L2 flush, scattered slots."""
+    from qwenedit_b200.paged import PagedKVPool
+
+    layers, kvh, hd, hidden, n = 28, 4, 128, 3584, 1024
+    pool = PagedKVPool("encoder", layers, kvh, hd, 4 << 30, torch.bfloat16, device, extra_dim=hidden)
+    pool.index.shuffle_free(77)
+    slots = pool.alloc(n)
+    pool.write(slots, torch.randn(layers, 2, n, kvh, hd, device=device).bfloat16())
+    pool.write_extra(slots, torch.randn(n, hidden, device=device).bfloat16())
+    out_kv = torch.empty(layers, 2, n, kvh, hd, dtype=torch.bfloat16, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    kv_ms = _time_kernel(lambda: pool.gather_into(slots, out_kv), flush)
+    hid_ms = _time_kernel(lambda: pool.gather_extra(slots), flush)
+    kv_bytes = 2 * layers * 2 * n * kvh * hd * 2
+    hid_bytes = 2 * n * hidden * 2
+    if pool.device_errors():
+        raise RuntimeError("encoder gather reported an error")
+    return {"kv_gather_ms": round(kv_ms, 4), "kv_GB/s": round(kv_bytes / kv_ms / 1e6, 1),
+            "hidden_gather_ms": round(hid_ms, 4), "hidden_GB/s": round(hid_bytes / hid_ms / 1e6, 1),
+            "bytes": {"kv": kv_bytes, "hidden": hid_bytes}, "note": "single launches: launch latency included"}
 
 
 def latent_extras(device):

@@ -142,6 +142,10 @@ int qe_set_norm_table_mode(int32_t mode);
  * No counterpart in the reference; for measurement and tests. */
 int qe_set_silu_table_mode(int32_t mode);
 
+/* SiLU kernel load schedule (process-wide): 1 = the next items' loads are issued before the current ones are
+ * computed (default), 0 = load then compute. Results are identical. No counterpart in the reference. */
+int qe_set_silu_pipeline(int32_t on);
+
 /* Fill `table` (65,536 uint16, 16-byte aligned device memory) with bf16(silu(g)) for every bf16 bit pattern g:
  * bf16(g / (1 + exp(-g))) exactly as the fused kernel's arithmetic rounds it (fibo/fp4.py:90). Build it once
  * per device; it is the workspace of qe_silu_mul_fp4. */

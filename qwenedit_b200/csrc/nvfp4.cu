@@ -737,6 +737,8 @@ std::atomic<int> g_silu_table_mode{0};
 // by size: the L1 form below this many rows (no 128 KiB staging per CTA; device time 5.4 vs 8.1 us at one
 // row, equal at 1,024, slower from 4,096 rows: 54.6 vs 50.4 us, K = 12288)
 constexpr int64_t kSiluL1Rows = 1024;
+// 1: next-iteration loads issued before the current items are computed (512-thread CTAs); 0: 1024 threads
+std::atomic<int> g_silu_pipeline{1};
 
 // Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
 // multiple of 64 takes the runtime-K kernel.
@@ -788,16 +790,20 @@ __device__ __forceinline__ uint32_t silu_lookup_l1(const uint16_t *tab, uint32_t
 }
 
 // A warp item is 32 consecutive 16-value groups of one row, one group per lane; kSiluItems items per
-// iteration so every lane has 8 16-byte loads in flight before it computes. kAmax: the calibration pre-pass —
-// the same y, reduced to max |y| instead of quantised and stored.
+// iteration, so every lane has 8 16-byte loads of them in flight. With kPipe the loads of the next iteration's
+// items are issued before the current ones are computed (512 threads per CTA, so 16 loads per lane can be in
+// flight: the global-load latency is hidden behind the lookups and the quantisation); without, 1024 threads
+// load, then compute. Items are tracked as (row, 32-group segment) and advanced without division.
 // kL1: the SiLU table is read from global memory through the L1 cache instead of being staged in shared
 // memory (no 128 KiB copy per CTA before the first row; lookups of the values a row actually uses stay in L1).
-template <bool kAmax, bool kL1>
-__global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
+// kAmax: the calibration pre-pass — the same y, reduced to max |y| instead of quantised and stored.
+template <bool kAmax, bool kL1, bool kPipe>
+__global__ void __launch_bounds__(kPipe ? kSiluThreads / 2 : kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
+  constexpr int kThreads = kPipe ? kSiluThreads / 2 : kSiluThreads;
   extern __shared__ uint4 tab4[];
   float *scale_tab = reinterpret_cast<float *>(tab4 + (kL1 ? 0 : kSiluTable / 8));
   if (!kL1)
-    for (int i = threadIdx.x; i < kSiluTable / 8; i += kSiluThreads) tab4[i] = __ldg(p.table + i);
+    for (int i = threadIdx.x; i < kSiluTable / 8; i += kThreads) tab4[i] = __ldg(p.table + i);
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
   if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
   __syncthreads();
@@ -805,48 +811,87 @@ __global__ void __launch_bounds__(kSiluThreads, 1) silu_mul_fp4_kernel(SiluParam
   const int lane = threadIdx.x & 31;
   const int gpr = int(p.K >> 4);
   const int segs = (gpr + 31) >> 5;
-  const int64_t items = p.M * segs;
   const int64_t warp = int64_t(threadIdx.x >> 5) * gridDim.x + blockIdx.x;  // CTA-minor: items spread over SMs
-  const int64_t nwarps = (int64_t(gridDim.x) * kSiluThreads) >> 5;
+  const int64_t nwarps = int64_t(gridDim.x) * (kThreads >> 5);
+  const int64_t drow = nwarps / segs;
+  const int dseg = int(nwarps - drow * segs);
   uint32_t amax_w = 0u;  // kAmax: running bf16x2 max of |y|
 
-  for (int64_t it0 = warp; it0 < items; it0 += nwarps * kSiluItems) {
-    uint4 ga[kSiluItems], gb[kSiluItems], va[kSiluItems], vb[kSiluItems];
-    int64_t row[kSiluItems];
-    int grp[kSiluItems];
+  struct Item {
+    int64_t row;
+    int seg;
+  };
+  auto next = [&](Item it) {  // the item nwarps further on
+    it.row += drow;
+    it.seg += dseg;
+    if (it.seg >= segs) {
+      it.seg -= segs;
+      ++it.row;
+    }
+    return it;
+  };
+  struct Data {
+    uint4 ga, gb, va, vb;
+  };
+  auto valid = [&](const Item &it) { return it.row < p.M && it.seg * 32 + lane < gpr; };
+  auto load = [&](const Item &it, Data &d) {
+    if (valid(it)) {
+      const int64_t c = it.row * (p.K >> 3) + 2 * (it.seg * 32 + lane);
+      d.ga = ld16(p.gate + c);
+      d.gb = ld16(p.gate + c + 1);
+      d.va = ld16(p.value + c);
+      d.vb = ld16(p.value + c + 1);
+    }
+  };
+  auto compute = [&](const Item &it, const Data &d) {
+    if (!valid(it)) return;
+    const int grp = it.seg * 32 + lane;
+    uint32_t gw[8], vw[8], y[8];
+    unpack16(d.ga, d.gb, gw);
+    unpack16(d.va, d.vb, vw);
 #pragma unroll
-    for (int u = 0; u < kSiluItems; ++u) {
-      const int64_t it = it0 + int64_t(u) * nwarps;
-      row[u] = it / segs;
-      grp[u] = int(it - row[u] * segs) * 32 + lane;
-      if (it < items && grp[u] < gpr) {
-        const int64_t c = row[u] * (p.K >> 3) + 2 * grp[u];
-        ga[u] = ld16(p.gate + c);
-        gb[u] = ld16(p.gate + c + 1);
-        va[u] = ld16(p.value + c);
-        vb[u] = ld16(p.value + c + 1);
-      }
+    for (int i = 0; i < 8; ++i) {  // bf16(silu(g) * v)
+      y[i] = bmul2(kL1 ? silu_lookup_l1(tab, gw[i]) : silu_lookup(tab, gw[i]), vw[i]);
+    }
+    if constexpr (kAmax) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax_w = bamax2(amax_w, y[i]);
+    } else {
+      uint32_t sb;
+      const uint2 codes = quantize16(y, gs, scale_tab, sb);
+      *reinterpret_cast<uint2 *>(p.q + it.row * (p.K >> 1) + int64_t(grp) * 8) = codes;
+      p.sf[sf_offset(it.row, grp, p.K)] = uint8_t(sb);
+    }
+  };
+
+  Item cur[kSiluItems];
+  cur[0] = Item{warp / segs, int(warp % segs)};
+#pragma unroll
+  for (int u = 1; u < kSiluItems; ++u) cur[u] = next(cur[u - 1]);
+  Data dc[kSiluItems];
+  if constexpr (kPipe) {
+#pragma unroll
+    for (int u = 0; u < kSiluItems; ++u) load(cur[u], dc[u]);
+  }
+  while (cur[0].row < p.M) {
+    Item nx[kSiluItems];
+    nx[0] = next(cur[kSiluItems - 1]);
+#pragma unroll
+    for (int u = 1; u < kSiluItems; ++u) nx[u] = next(nx[u - 1]);
+    Data dn[kSiluItems];
+    if constexpr (kPipe) {
+#pragma unroll
+      for (int u = 0; u < kSiluItems; ++u) load(nx[u], dn[u]);  // next iteration's loads go out first
+    } else {
+#pragma unroll
+      for (int u = 0; u < kSiluItems; ++u) load(cur[u], dc[u]);
     }
 #pragma unroll
+    for (int u = 0; u < kSiluItems; ++u) compute(cur[u], dc[u]);
+#pragma unroll
     for (int u = 0; u < kSiluItems; ++u) {
-      const int64_t it = it0 + int64_t(u) * nwarps;
-      if (!(it < items && grp[u] < gpr)) continue;
-      uint32_t gw[8], vw[8], y[8];
-      unpack16(ga[u], gb[u], gw);
-      unpack16(va[u], vb[u], vw);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {  // bf16(silu(g) * v)
-        y[i] = bmul2(kL1 ? silu_lookup_l1(tab, gw[i]) : silu_lookup(tab, gw[i]), vw[i]);
-      }
-      if constexpr (kAmax) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax_w = bamax2(amax_w, y[i]);
-      } else {
-        uint32_t sb;
-        const uint2 codes = quantize16(y, gs, scale_tab, sb);
-        *reinterpret_cast<uint2 *>(p.q + row[u] * (p.K >> 1) + int64_t(grp[u]) * 8) = codes;
-        p.sf[sf_offset(row[u], grp[u], p.K)] = uint8_t(sb);
-      }
+      cur[u] = nx[u];
+      if constexpr (kPipe) dc[u] = dn[u];
     }
   }
   if constexpr (kAmax) {
@@ -995,6 +1040,12 @@ int qe_set_silu_table_mode(int32_t mode) {
   return qe::ok();
 }
 
+int qe_set_silu_pipeline(int32_t on) {
+  if (on < 0 || on > 1) return fail(QE_ERR_INVALID, "qe_set_silu_pipeline: 0 or 1");
+  qe::g_silu_pipeline.store(on, std::memory_order_relaxed);
+  return qe::ok();
+}
+
 int qe_set_norm_table_mode(int32_t mode) {
   if (mode < 0 || mode > 1) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0 or 1");
   qe::g_norm_table_mode.store(mode, std::memory_order_relaxed);
@@ -1045,24 +1096,31 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.padded = padded;
   const int mode = g_silu_table_mode.load(std::memory_order_relaxed);
   const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
+  const bool pipe = g_silu_pipeline.load(std::memory_order_relaxed) != 0;
   const size_t smem = (l1 ? 0 : size_t(kSiluTable) * 2) + kScaleTab * sizeof(float);
-  static bool attr_set[4][64] = {};
+  static bool attr_set[8][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  auto kernel = amax ? (l1 ? silu_mul_fp4_kernel<true, true> : silu_mul_fp4_kernel<true, false>)
-                     : (l1 ? silu_mul_fp4_kernel<false, true> : silu_mul_fp4_kernel<false, false>);
-  const int variant = (amax ? 2 : 0) + (l1 ? 1 : 0);
+  using Kernel = void (*)(SiluParams);
+  static const Kernel kernels[8] = {
+      silu_mul_fp4_kernel<false, false, false>, silu_mul_fp4_kernel<false, true, false>,
+      silu_mul_fp4_kernel<true, false, false>,  silu_mul_fp4_kernel<true, true, false>,
+      silu_mul_fp4_kernel<false, false, true>,  silu_mul_fp4_kernel<false, true, true>,
+      silu_mul_fp4_kernel<true, false, true>,   silu_mul_fp4_kernel<true, true, true>};
+  const int variant = (pipe ? 4 : 0) + (amax ? 2 : 0) + (l1 ? 1 : 0);
+  const Kernel kernel = kernels[variant];
+  const int threads = pipe ? kSiluThreads / 2 : kSiluThreads;
   if (!attr_set[variant][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_fp4: smem attribute");
     attr_set[variant][dev] = true;
   }
   const int64_t items = M * ((K / 16 + 31) / 32);  // warp items: 32 groups of one row
-  const int64_t warps_per_block = kSiluThreads / 32;
+  const int64_t warps_per_block = threads / 32;
   const int64_t pad_items = amax ? 0 : (padded - M) * (K / 64) / 32;
   int64_t blocks = (std::max<int64_t>(items, pad_items) + warps_per_block - 1) / warps_per_block;
   blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count())));
-  kernel<<<dim3(unsigned(blocks)), dim3(kSiluThreads), smem, st>>>(p);
+  kernel<<<dim3(unsigned(blocks)), dim3(threads), smem, st>>>(p);
   return cuda_status(cudaGetLastError(), "qe_silu_mul_fp4 launch");
 }
 }  // namespace

@@ -110,13 +110,16 @@ def test_norm_scale_k3072_table_layouts(B, masked, shift, table_mode):
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
 
-@pytest.fixture(params=[1, 2], ids=["smem_table", "l1_table"])
+@pytest.fixture(params=[(1, 1), (2, 1), (1, 0)], ids=["smem_table", "l1_table", "smem_table_unpipelined"])
 def silu_mode(request):
-    """Both homes of the SiLU table (staged in shared memory, or read through L1)."""
+    """Both homes of the SiLU table (staged in shared memory, or read through L1) and both load schedules."""
     from qwenedit_b200 import _lib
-    _lib.call("qe_set_silu_table_mode", request.param)
+    table, pipe = request.param
+    _lib.call("qe_set_silu_table_mode", table)
+    _lib.call("qe_set_silu_pipeline", pipe)
     yield request.param
     _lib.call("qe_set_silu_table_mode", 0)
+    _lib.call("qe_set_silu_pipeline", 1)
 
 
 @pytest.mark.parametrize("M,K", [(4096, 12288), (300, 9536), (1, 64), (129, 640)])
