@@ -24,6 +24,7 @@ from __future__ import annotations
 import ctypes
 import hashlib
 import json
+import logging
 from ctypes import c_void_p
 
 import torch
@@ -31,6 +32,8 @@ import torch.distributed as dist
 
 from qwenedit_b200 import _lib
 from qwenedit_b200.paged import PagedKVPool, pool_geometry
+
+logger = logging.getLogger(__name__)
 
 _IPC_HANDLE_BYTES = 64
 
@@ -197,7 +200,10 @@ class HeadShardedKVPool:
         return self.pool.device_errors()
 
     def close(self) -> None:
-        """Unmap the peers' pools, then free this rank's (every rank must call it; collective)."""
+        """Unmap the peers' pools, then free this rank's (every rank must call it; collective). Tensors returned
+        by ``gather`` as views of the pool are invalid afterwards."""
+        if self._own is None:
+            return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         for m in self._peers:
@@ -207,6 +213,14 @@ class HeadShardedKVPool:
         dist.barrier(group=self.group)
         self.pool = None
         self._own.close()
+        self._own = None
+
+    def __del__(self):
+        # releasing the memory needs the other ranks (they may still map it), so it is never done here: a pool
+        # dropped without close() keeps its allocation until the process exits
+        if getattr(self, "_own", None) is not None:
+            logger.warning("HeadShardedKVPool %r dropped without close(); its device memory is held until exit",
+                           getattr(self.pool, "name", "?"))
 
 
 __all__ = ["HeadShardedKVPool", "exchange", "index_digest", "verify_replicas"]
