@@ -105,9 +105,10 @@ int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *
                                  int32_t n_planes, int64_t row_bytes, const int64_t *slots, int64_t n_tokens,
                                  int32_t *err_flag, void *stream);
 
-/* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel,
- * 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned rows of <= 32 KiB,
- * else the warp kernel). No counterpart in the reference; for measurement and tuning. */
+/* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel (rows of at
+ * most 1 KiB are moved several per warp pass), 2 = TMA bulk-copy pipeline (cp.async.bulk through
+ * shared memory; 16-byte aligned rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per
+ * warp pass whatever the row size. No counterpart in the reference; for measurement and tuning. */
 int qe_set_paged_copy_mode(int32_t mode);
 
 /* ---- fused NVFP4 activation quantisers (device) ---------------------------------------------

@@ -147,11 +147,12 @@ def _slots_tensor(host: np.ndarray, pool: "PagedKVPool") -> torch.Tensor:
     return t
 
 
-COPY_MODES = {"auto": 0, "warp": 1, "bulk": 2}
+COPY_MODES = {"auto": 0, "warp": 1, "bulk": 2, "warp_row": 3}
 
 
 def set_copy_mode(mode: str) -> None:
-    """Select the paged copy kernel process-wide: "auto", "warp" (vectorised LDG/STG) or "bulk" (TMA bulk copies)."""
+    """Select the paged copy kernel process-wide: "auto", "warp" (vectorised LDG/STG, short rows several per warp
+    pass), "bulk" (TMA bulk copies) or "warp_row" (the warp kernel, one row per warp pass)."""
     _lib.call("qe_set_paged_copy_mode", COPY_MODES[mode])
 
 

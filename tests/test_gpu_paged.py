@@ -14,9 +14,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-@pytest.fixture(autouse=True, params=["warp", "bulk"])
+@pytest.fixture(autouse=True, params=["warp", "warp_row", "bulk"])
 def copy_kernel(request):
-    """Run every test with both paged-copy kernels (vectorised warp copy, TMA bulk pipeline)."""
+    """Run every test with every paged-copy kernel (vectorised warp copy, several short rows per warp pass or one
+    row per pass, TMA bulk pipeline)."""
     from qwenedit_b200.paged import set_copy_mode
 
     set_copy_mode(request.param)
@@ -64,6 +65,25 @@ def test_gather_through_block_table_bit_exact(page):
     assert getattr(slots, "_qe_pages", None) is not None  # the block-table kernel ran
     ref = pool.kv.cpu().index_select(2, torch.from_numpy(host))
     assert torch.equal(out.cpu(), ref)
+
+
+@pytest.mark.parametrize("H,page", [(3, 64), (6, 64), (12, 16), (4, 1), (1, 1), (24, 64)])
+def test_short_rows_gather_and_append(H, page):
+    """Row sizes of the head-sharded DiT pools (3 / 6 / 12 of 24 heads: 768 B - 3 KiB), the encoder (4 heads, 1 KiB)
+    and tiny rows, through block tables and slot lists, with a token count that is no multiple of the rows moved
+    per warp pass."""
+    L, D = 3, 128
+    pool = _pool(L, H, D, 64 * 30, torch.bfloat16, page=page, seed=H * 7 + page)
+    pool.index.shuffle_free(H + page)
+    n = 64 * 11 + 37
+    slots = pool.alloc(n)
+    new = inputs.f32(H + 3, (L, 2, n, H, D)).to(torch.bfloat16)
+    pool.write(slots, new.to(DEV))
+    ref = pool.kv.cpu().clone()
+    ref.index_copy_(2, torch.from_numpy(slots._qe_host), new)
+    assert torch.equal(pool.kv.cpu(), ref)
+    out = pool.gather(slots)
+    assert torch.equal(out.cpu(), new) and pool.device_errors() == 0
 
 
 def test_contiguous_run_is_a_view():
