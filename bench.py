@@ -415,11 +415,33 @@ def encoder_extras(device, peak):
     hid_ms = _time_kernel(lambda: pool.gather_extra(slots), flush)
     kv_bytes = 2 * layers * 2 * n * kvh * hd * 2
     hid_bytes = 2 * n * hidden * 2
+    # partial hit (encoder.py:173-182): the prefix K/V head-major with room for a 256-token tail, in one launch,
+    # against the reference's gather followed by a transpose + cat per layer and K/V (torch ops on our gather)
+    tail = 256
+    k_tail = torch.randn(1, kvh, tail, hd, device=device).bfloat16()
+
+    def ours():
+        buf = pool.gather_heads(slots, n + tail)
+        for layer in range(layers):
+            buf[layer, 0, :, n:] = k_tail[0]
+            buf[layer, 1, :, n:] = k_tail[0]
+
+    def reference_ops():
+        cached = pool.gather(slots)
+        for layer in range(layers):
+            torch.cat([cached[layer, 0].transpose(0, 1)[None], k_tail], dim=2)
+            torch.cat([cached[layer, 1].transpose(0, 1)[None], k_tail], dim=2)
+
+    tail_ms = _time_graph([ours])
+    tail_ref_ms = _time_graph([reference_ops])
     if pool.device_errors():
         raise RuntimeError("encoder gather reported an error")
     return {"kv_gather_ms": round(kv_ms, 4), "kv_GB/s": round(kv_bytes / kv_ms / 1e6, 1),
             "hidden_gather_ms": round(hid_ms, 4), "hidden_GB/s": round(hid_bytes / hid_ms / 1e6, 1),
-            "bytes": {"kv": kv_bytes, "hidden": hid_bytes}, "note": "single launches: launch latency included"}
+            "bytes": {"kv": kv_bytes, "hidden": hid_bytes}, "note": "single launches: launch latency included",
+            "partial_hit_prefix_ms": {"gather_heads_plus_tail_writes": round(tail_ms, 4),
+                                      "gather_then_per_layer_transpose_cat": round(tail_ref_ms, 4),
+                                      "prefix_tokens": n, "tail_tokens": tail, "timing": "CUDA graph, device time"}}
 
 
 def latent_extras(device):

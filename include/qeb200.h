@@ -105,6 +105,16 @@ int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *
                                  int32_t n_planes, int64_t row_bytes, const int64_t *slots, int64_t n_tokens,
                                  int32_t *err_flag, void *stream);
 
+/* Gather into a head-major layout with room for a tail (the text encoder's partial hit, cache/encoder.py:173-182,
+ * which gathers [L, 2, m, H, D] and then builds [1, H, m + n, D] per layer by transpose + cat): for every plane
+ * p, token t < n_tokens and head h, the head_bytes of head h of pool row slots[t] go to
+ *   out.plane(p) + h * out_head_stride + t * out_token_stride.
+ * row_bytes = heads * head_bytes; everything 16-byte aligned. Slots outside [0, pool_rows) are skipped and set
+ * *err_flag. No counterpart as such in the reference (it is index_select + transpose + cat). */
+int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
+                          int64_t head_bytes, int64_t out_head_stride, int64_t out_token_stride, const int64_t *slots,
+                          int64_t n_tokens, int32_t *err_flag, void *stream);
+
 /* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel (rows of at
  * most 1 KiB are moved several per warp pass), 2 = TMA bulk-copy pipeline (cp.async.bulk through
  * shared memory; 16-byte aligned rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per

@@ -53,6 +53,8 @@ SIGNATURES: dict[str, list] = {
     "qe_latent_compose": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                           c_int64, c_void_p],
     "qe_latent_crop": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "qe_gather_slots_heads": [Planes, c_int64, Planes, c_int32, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                              c_int64, c_void_p, c_void_p],
     "qe_ipc_alloc": [c_int64, POINTER(c_void_p), c_void_p],
     "qe_ipc_free": [c_void_p],
     "qe_ipc_open": [c_void_p, POINTER(c_void_p)],

@@ -191,6 +191,72 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
   }
 }
 
+// Gather into a head-major layout with room for a tail: out[plane][h][t] (head stride and token stride free)
+// = pool row slots[t] of plane, head h. For the text encoder's partial hit (cache/encoder.py:173-182), which
+// gathers the prefix [L, 2, m, H, D] and then, per layer, transposes it and concatenates the tail K/V into a
+// fresh [1, H, m + n, D] tensor: written here once, straight into a [L, 2, H, m + n, D] buffer whose last n
+// positions the caller fills per layer. One warp moves R consecutive tokens of one plane per pass (16-byte
+// vectors, 16 per lane in flight); lane i < R holds token i's slot.
+struct HeadsParams {
+  Planes pool;
+  Planes out;
+  int64_t pool_rows, n_tokens, row_bytes, head_bytes, out_head_stride, out_token_stride;
+  const int64_t *slots;
+  int32_t n_planes, rows_per_pass;
+  int32_t *err;
+};
+
+__global__ void __launch_bounds__(kThreads) gather_heads_kernel(HeadsParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * kThreads) >> 5;
+  const int64_t vpr = p.row_bytes / 16, vph = p.head_bytes / 16;
+  const int R = p.rows_per_pass;
+  const int64_t blocks_per_plane = (p.n_tokens + R - 1) / R;
+  const int64_t items = int64_t(p.n_planes) * blocks_per_plane;
+  for (int64_t it = warp; it < items; it += nwarps) {
+    const int32_t plane = int32_t(it / blocks_per_plane);
+    const int64_t t0 = (it - int64_t(plane) * blocks_per_plane) * R;
+    int64_t my_slot = -1;
+    if (lane < R && t0 + lane < p.n_tokens) {
+      my_slot = __ldg(p.slots + t0 + lane);
+      if (my_slot < 0 || my_slot >= p.pool_rows) {
+        if (p.err) atomicOr(p.err, 1);
+        my_slot = -2;
+      }
+    }
+    const char *pool_plane = p.pool.plane(plane);
+    char *out_plane = p.out.plane(plane);
+    for (int64_t base = 0; base < int64_t(R) * vpr; base += 32 * kRowsUnroll) {
+      // (row, head, vector-in-head) of vector base + lane, advanced by 32 per k
+      int64_t v = base + lane;
+      int ri = int(v / vpr);
+      int64_t vin = v - int64_t(ri) * vpr;
+      int4 buf[kRowsUnroll];
+      int4 *dst_at[kRowsUnroll];
+#pragma unroll
+      for (int k = 0; k < kRowsUnroll; ++k) {
+        const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
+        dst_at[k] = nullptr;
+        if (ri < R && slot >= 0) {
+          const int64_t h = vin / vph, w = vin - h * vph;
+          buf[k] = ld_stream(reinterpret_cast<const int4 *>(pool_plane + slot * p.row_bytes) + vin);
+          dst_at[k] = reinterpret_cast<int4 *>(out_plane + h * p.out_head_stride + (t0 + ri) * p.out_token_stride) + w;
+        }
+        vin += 32;
+        while (vin >= vpr) {
+          vin -= vpr;
+          ++ri;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kRowsUnroll; ++k) {
+        if (dst_at[k]) *dst_at[k] = buf[k];
+      }
+    }
+  }
+}
+
 // ---- TMA bulk-copy variant --------------------------------------------------------------------
 // One elected thread per CTA drives the copy engine: cp.async.bulk global->shared (completion counted in
 // bytes on a per-stage mbarrier) then cp.async.bulk shared->global, kStages chunks of up to kChunk bytes in
@@ -635,6 +701,41 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
   // Source pointers are only known on the device; the Python side checks each one for 16-byte
   // alignment before uploading the array, so the width follows the pool and the row size.
   s = qe::launch<qe::kSlots, false, true>(p, qe::align_of(pool, nullptr, row_bytes), static_cast<cudaStream_t>(stream));
+  return s ? s : qe::ok();
+}
+
+int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
+                          int64_t head_bytes, int64_t out_head_stride, int64_t out_token_stride, const int64_t *slots,
+                          int64_t n_tokens, int32_t *err_flag, void *stream) {
+  QE_CHECK_ARG(n_planes >= 1 && pool_rows >= 1 && n_tokens >= 0, "qe_gather_slots_heads: bad sizes");
+  QE_CHECK_ARG(head_bytes > 0 && head_bytes % 16 == 0 && row_bytes % head_bytes == 0,
+               "qe_gather_slots_heads: head_bytes must be a multiple of 16 dividing row_bytes");
+  QE_CHECK_ARG(out_head_stride % 16 == 0 && out_token_stride % 16 == 0 && out_head_stride >= 0 && out_token_stride >= 0,
+               "qe_gather_slots_heads: output strides must be non-negative multiples of 16 bytes");
+  QE_CHECK_ARG(pool.planes_inner >= 1 && out.planes_inner >= 1, "qe_gather_slots_heads: planes_inner must be >= 1");
+  QE_CHECK_ARG(pool.base && out.base && qe::planes_aligned(pool, 16) && qe::planes_aligned(out, 16),
+               "qe_gather_slots_heads: planes must be 16-byte aligned");
+  QE_CHECK_ARG(n_tokens == 0 || slots, "qe_gather_slots_heads: null slots");
+  if (n_tokens == 0) return qe::ok();
+  qe::HeadsParams p{};
+  p.pool = qe::to_planes(pool);
+  p.out = qe::to_planes(out);
+  p.pool_rows = pool_rows;
+  p.n_tokens = n_tokens;
+  p.row_bytes = row_bytes;
+  p.head_bytes = head_bytes;
+  p.out_head_stride = out_head_stride;
+  p.out_token_stride = out_token_stride;
+  p.slots = slots;
+  p.n_planes = n_planes;
+  p.rows_per_pass = int32_t(std::max<int64_t>(1, std::min<int64_t>(32 * qe::kRowsUnroll / (row_bytes / 16), 32)));
+  p.err = err_flag;
+  const int64_t items = int64_t(n_planes) * ((n_tokens + p.rows_per_pass - 1) / p.rows_per_pass);
+  const int64_t warps_per_block = qe::kThreads / 32;
+  int64_t blocks = std::min<int64_t>((items + warps_per_block - 1) / warps_per_block, int64_t(qe::sm_count()) * 8);
+  blocks = std::max<int64_t>(blocks, 1);
+  qe::gather_heads_kernel<<<dim3(unsigned(blocks)), dim3(qe::kThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
+  int s = qe::cuda_status(cudaGetLastError(), "qe_gather_slots_heads launch");
   return s ? s : qe::ok();
 }
 

@@ -328,6 +328,30 @@ class PagedKVPool:
             self._copy("gather", self.kv, out, indices, host, n_planes=2 * self.layers)
         return out
 
+    def gather_heads(self, indices: torch.Tensor, length: int | None = None) -> torch.Tensor:
+        """K/V of `indices` head-major with room for a tail: [L, 2, H, length, D] (length >= n, default n), the
+        first n positions filled from the pool, the rest left for the caller. For the text encoder's partial hit
+        (encoder.py:173-182): write layer l's tail K/V into ``buf[l, :, :, m:]`` and attend over ``buf[l, 0][None]``
+        / ``buf[l, 1][None]`` instead of transposing and concatenating the prefix every layer. One launch."""
+        host = self._host_slots(indices)
+        n = len(host)
+        length = n if length is None else int(length)
+        if length < n:
+            raise ValueError(f"length {length} is shorter than the {n} gathered tokens")
+        out = torch.empty(self.layers, 2, self.heads, length, self.head_dim, dtype=self.kv.dtype, device=self.device)
+        if n:
+            self._require_cuda(indices)
+            e = self.kv.element_size()
+            pool = _lib.planes(self.kv.data_ptr(), self.kv.stride(0) * e, self.kv.stride(1) * e, 2)
+            oth = _lib.planes(out.data_ptr(), out.stride(0) * e, out.stride(1) * e, 2)
+            slots = indices if indices.dtype == torch.int64 else indices.to(torch.int64)
+            slots = slots.contiguous()
+            with torch.cuda.device(self.device):
+                _lib.call("qe_gather_slots_heads", pool, self.rows, oth, 2 * self.layers, self._row_bytes(self.kv),
+                          self.head_dim * e, out.stride(2) * e, out.stride(3) * e, slots.data_ptr(), n,
+                          self._err.data_ptr(), self._stream())
+        return out
+
     def write(self, indices: torch.Tensor, kv: torch.Tensor) -> None:
         """Scatter kv [L, 2, n, H, D] into pool rows `indices` (index_copy_ along dim 2)."""
         if kv.dtype != self.kv.dtype:

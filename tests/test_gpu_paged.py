@@ -86,6 +86,28 @@ def test_short_rows_gather_and_append(H, page):
     assert torch.equal(out.cpu(), new) and pool.device_errors() == 0
 
 
+@pytest.mark.parametrize("H,D,page", [(4, 128, 1), (24, 128, 64), (3, 64, 1), (1, 8, 4)])
+def test_gather_heads_is_transposed_gather_with_room(H, D, page):
+    """gather_heads == index_select then [L, 2, H, n, D] with `length - n` free positions; and the encoder's
+    per-layer transpose + cat of the prefix with a tail (encoder.py:178-180) equals the buffer with the tail
+    written in place."""
+    L = 3
+    pool = _pool(L, H, D, 64 * 20, torch.bfloat16, page=page, seed=H + D)
+    pool.index.shuffle_free(H * D)
+    m, n = 333, 45
+    idx = pool.alloc(m)
+    buf = pool.gather_heads(idx, m + n)
+    assert buf.shape == (L, 2, H, m + n, D) and pool.device_errors() == 0
+    ref = pool.kv.cpu().index_select(2, torch.from_numpy(idx._qe_host)).permute(0, 1, 3, 2, 4)
+    assert torch.equal(buf[:, :, :, :m].cpu(), ref)
+    cached = pool.gather(idx)
+    for layer in range(L):
+        k = inputs.f32(layer, (1, H, n, D)).to(torch.bfloat16).to(DEV)
+        want = torch.cat([cached[layer, 0].transpose(0, 1)[None], k], dim=2)
+        buf[layer, 0, :, m:] = k[0]
+        assert torch.equal(buf[layer, 0][None], want)
+
+
 def test_contiguous_run_is_a_view():
     """tests/test_paged.py:58-65."""
     pool = PagedKVPool("t", 2, 1, 4, 64 * 32, torch.bfloat16, DEV)
