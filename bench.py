@@ -110,7 +110,7 @@ class ClockSampler(threading.Thread):
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.05)
+            time.sleep(0.01)  # ~10 samples over a 0.1 s timed region
 
     def stop(self) -> dict:
         self._halt.set()
