@@ -2,8 +2,6 @@
 with RuntimeError (there is no CPU path), bad boxes / dtypes / shapes raise before any launch, and the C ABI
 rejects bad sizes with QE_ERR_INVALID (ValueError) without touching the GPU."""
 
-
-
 import pytest
 import torch
 
