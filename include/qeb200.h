@@ -153,8 +153,9 @@ int qe_set_norm_table_mode(int32_t mode);
  * No counterpart in the reference; for measurement and tests. */
 int qe_set_silu_table_mode(int32_t mode);
 
-/* SiLU kernel load schedule (process-wide): 1 = the next items' loads are issued before the current ones are
- * computed (default), 0 = load then compute. Results are identical. No counterpart in the reference. */
+/* SiLU kernel load schedule (process-wide): 0 = load then compute (1024 threads per CTA); 1 = the next item's
+ * loads issued before the current one is computed (1024 threads; default); 2 = the same with two items per
+ * iteration (512 threads). Results are identical. No counterpart in the reference. */
 int qe_set_silu_pipeline(int32_t on);
 
 /* Fill `table` (65,536 uint16, 16-byte aligned device memory) with bf16(silu(g)) for every bf16 bit pattern g:

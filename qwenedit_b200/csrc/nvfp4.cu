@@ -737,7 +737,8 @@ std::atomic<int> g_silu_table_mode{0};
 // by size: the L1 form below this many rows (no 128 KiB staging per CTA; device time 5.4 vs 8.1 us at one
 // row, equal at 1,024, slower from 4,096 rows: 54.6 vs 50.4 us, K = 12288)
 constexpr int64_t kSiluL1Rows = 1024;
-// 1: next-iteration loads issued before the current items are computed (512-thread CTAs); 0: 1024 threads
+// load schedule of the SiLU kernel: 0 = load then compute, 1 = pipelined with one item per iteration
+// (1024 threads), 2 = pipelined with two items per iteration (512 threads)
 std::atomic<int> g_silu_pipeline{1};
 
 // Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
@@ -780,7 +781,6 @@ struct SiluParams {
 };
 
 constexpr int kSiluThreads = 1024;  // one CTA per SM (the table takes 128 KiB of shared memory)
-constexpr int kSiluItems = 2;       // warp items (32 groups each) in flight per iteration
 
 __device__ __forceinline__ uint32_t silu_lookup(const uint16_t *tab, uint32_t w) {
   return uint32_t(tab[w & 0xffffu]) | (uint32_t(tab[w >> 16]) << 16);
@@ -789,17 +789,24 @@ __device__ __forceinline__ uint32_t silu_lookup_l1(const uint16_t *tab, uint32_t
   return uint32_t(__ldg(tab + (w & 0xffffu))) | (uint32_t(__ldg(tab + (w >> 16))) << 16);
 }
 
-// A warp item is 32 consecutive 16-value groups of one row, one group per lane; kSiluItems items per
-// iteration, so every lane has 8 16-byte loads of them in flight. With kPipe the loads of the next iteration's
-// items are issued before the current ones are computed (512 threads per CTA, so 16 loads per lane can be in
-// flight: the global-load latency is hidden behind the lookups and the quantisation); without, 1024 threads
-// load, then compute. Items are tracked as (row, 32-group segment) and advanced without division.
+// A warp item is 32 consecutive 16-value groups of one row, one group per lane (4 16-byte loads per lane).
+// With kPipe the loads of the next iteration's items are issued before the current ones are computed, so the
+// global-load latency is hidden behind the table lookups and the quantisation; without, the items are loaded,
+// then computed. Items are tracked as (row, 32-group segment) and advanced without division.
 // kL1: the SiLU table is read from global memory through the L1 cache instead of being staged in shared
 // memory (no 128 KiB copy per CTA before the first row; lookups of the values a row actually uses stay in L1).
 // kAmax: the calibration pre-pass — the same y, reduced to max |y| instead of quantised and stored.
-template <bool kAmax, bool kL1, bool kPipe>
-__global__ void __launch_bounds__(kPipe ? kSiluThreads / 2 : kSiluThreads, 1) silu_mul_fp4_kernel(SiluParams p) {
-  constexpr int kThreads = kPipe ? kSiluThreads / 2 : kSiluThreads;
+// kSched: 0 = load then compute (2 items, 1024 threads); 1 = pipelined, 1 item per iteration, 1024 threads
+// (the default: 32 warps per SM with 4 loads each in flight, 64 registers; 0.90 of HBM at T=16384 against
+// 0.87 for 2 = pipelined with 2 items per iteration and 512 threads, and 0.81 for 0).
+constexpr int silu_threads(int sched) { return sched == 2 ? kSiluThreads / 2 : kSiluThreads; }
+constexpr int silu_items(int sched) { return sched == 1 ? 1 : 2; }
+
+template <bool kAmax, bool kL1, int kSched>
+__global__ void __launch_bounds__(silu_threads(kSched), 1) silu_mul_fp4_kernel(SiluParams p) {
+  constexpr bool kPipe = kSched != 0;
+  constexpr int kThreads = silu_threads(kSched);
+  constexpr int kItems = silu_items(kSched);
   extern __shared__ uint4 tab4[];
   float *scale_tab = reinterpret_cast<float *>(tab4 + (kL1 ? 0 : kSiluTable / 8));
   if (!kL1)
@@ -864,32 +871,32 @@ __global__ void __launch_bounds__(kPipe ? kSiluThreads / 2 : kSiluThreads, 1) si
     }
   };
 
-  Item cur[kSiluItems];
+  Item cur[kItems];
   cur[0] = Item{warp / segs, int(warp % segs)};
 #pragma unroll
-  for (int u = 1; u < kSiluItems; ++u) cur[u] = next(cur[u - 1]);
-  Data dc[kSiluItems];
+  for (int u = 1; u < kItems; ++u) cur[u] = next(cur[u - 1]);
+  Data dc[kItems];
   if constexpr (kPipe) {
 #pragma unroll
-    for (int u = 0; u < kSiluItems; ++u) load(cur[u], dc[u]);
+    for (int u = 0; u < kItems; ++u) load(cur[u], dc[u]);
   }
   while (cur[0].row < p.M) {
-    Item nx[kSiluItems];
-    nx[0] = next(cur[kSiluItems - 1]);
+    Item nx[kItems];
+    nx[0] = next(cur[kItems - 1]);
 #pragma unroll
-    for (int u = 1; u < kSiluItems; ++u) nx[u] = next(nx[u - 1]);
-    Data dn[kSiluItems];
+    for (int u = 1; u < kItems; ++u) nx[u] = next(nx[u - 1]);
+    Data dn[kItems];
     if constexpr (kPipe) {
 #pragma unroll
-      for (int u = 0; u < kSiluItems; ++u) load(nx[u], dn[u]);  // next iteration's loads go out first
+      for (int u = 0; u < kItems; ++u) load(nx[u], dn[u]);  // next iteration's loads go out first
     } else {
 #pragma unroll
-      for (int u = 0; u < kSiluItems; ++u) load(cur[u], dc[u]);
+      for (int u = 0; u < kItems; ++u) load(cur[u], dc[u]);
     }
 #pragma unroll
-    for (int u = 0; u < kSiluItems; ++u) compute(cur[u], dc[u]);
+    for (int u = 0; u < kItems; ++u) compute(cur[u], dc[u]);
 #pragma unroll
-    for (int u = 0; u < kSiluItems; ++u) {
+    for (int u = 0; u < kItems; ++u) {
       cur[u] = nx[u];
       if constexpr (kPipe) dc[u] = dn[u];
     }
@@ -1041,7 +1048,7 @@ int qe_set_silu_table_mode(int32_t mode) {
 }
 
 int qe_set_silu_pipeline(int32_t on) {
-  if (on < 0 || on > 1) return fail(QE_ERR_INVALID, "qe_set_silu_pipeline: 0 or 1");
+  if (on < 0 || on > 2) return fail(QE_ERR_INVALID, "qe_set_silu_pipeline: 0, 1 or 2");
   qe::g_silu_pipeline.store(on, std::memory_order_relaxed);
   return qe::ok();
 }
@@ -1096,20 +1103,22 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.padded = padded;
   const int mode = g_silu_table_mode.load(std::memory_order_relaxed);
   const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
-  const bool pipe = g_silu_pipeline.load(std::memory_order_relaxed) != 0;
+  const int sched = g_silu_pipeline.load(std::memory_order_relaxed);
   const size_t smem = (l1 ? 0 : size_t(kSiluTable) * 2) + kScaleTab * sizeof(float);
-  static bool attr_set[8][64] = {};
+  static bool attr_set[12][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   using Kernel = void (*)(SiluParams);
-  static const Kernel kernels[8] = {
-      silu_mul_fp4_kernel<false, false, false>, silu_mul_fp4_kernel<false, true, false>,
-      silu_mul_fp4_kernel<true, false, false>,  silu_mul_fp4_kernel<true, true, false>,
-      silu_mul_fp4_kernel<false, false, true>,  silu_mul_fp4_kernel<false, true, true>,
-      silu_mul_fp4_kernel<true, false, true>,   silu_mul_fp4_kernel<true, true, true>};
-  const int variant = (pipe ? 4 : 0) + (amax ? 2 : 0) + (l1 ? 1 : 0);
+  static const Kernel kernels[12] = {
+      silu_mul_fp4_kernel<false, false, 0>, silu_mul_fp4_kernel<false, true, 0>,
+      silu_mul_fp4_kernel<true, false, 0>,  silu_mul_fp4_kernel<true, true, 0>,
+      silu_mul_fp4_kernel<false, false, 1>, silu_mul_fp4_kernel<false, true, 1>,
+      silu_mul_fp4_kernel<true, false, 1>,  silu_mul_fp4_kernel<true, true, 1>,
+      silu_mul_fp4_kernel<false, false, 2>, silu_mul_fp4_kernel<false, true, 2>,
+      silu_mul_fp4_kernel<true, false, 2>,  silu_mul_fp4_kernel<true, true, 2>};
+  const int variant = sched * 4 + (amax ? 2 : 0) + (l1 ? 1 : 0);
   const Kernel kernel = kernels[variant];
-  const int threads = pipe ? kSiluThreads / 2 : kSiluThreads;
+  const int threads = silu_threads(sched);
   if (!attr_set[variant][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_fp4: smem attribute");

@@ -110,7 +110,8 @@ def test_norm_scale_k3072_table_layouts(B, masked, shift, table_mode):
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
 
-@pytest.fixture(params=[(1, 1), (2, 1), (1, 0)], ids=["smem_table", "l1_table", "smem_table_unpipelined"])
+@pytest.fixture(params=[(1, 1), (2, 1), (1, 2), (1, 0)],
+                ids=["smem_table", "l1_table", "smem_table_two_items", "smem_table_unpipelined"])
 def silu_mode(request):
     """Both homes of the SiLU table (staged in shared memory, or read through L1) and both load schedules."""
     from qwenedit_b200 import _lib
