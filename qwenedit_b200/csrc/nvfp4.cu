@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
                 "TMEM tables need a compile-time K of whole 512-column blocks and four warps");
   constexpr bool kTables = kTab == 1;
   constexpr bool kTmem = kTab == 2;
+
   extern __shared__ uint4 smem[];
   constexpr int kP = kK ? pow2_at_least(kK) : 0;
   constexpr int kLeafLen = kP >= 128 ? 128 : kP;
@@ -521,17 +522,12 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   // chunk index of x chunk 2g (g = lane + 32 i) inside a row buffer: swz(2 (lane + 32 i)) written out
   const int x_lane = ((lane >> 3) << 4) + ((2 * lane & 15) ^ (lane >> 3) ^ ((lane >> 2) & 1));
 
-  int cur = 0;
-  for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1, advance()) {
-    fetch(m + nwarps, bufs + (cur ^ 1) * row_chunks);
-    cp_async_wait_1();  // this row's copies (all but the newest group) have landed
-    __syncwarp();
+  // one row: quantise (or reduce, kAmax) row m held in shared memory at row_s
+  auto row_body = [&](int64_t m, const uint4 *row_s) {
     if (m >= p.M) {  // padding rows of the last 128-row tile: zero scales, no codes
       if (!kAmax) zero_sf_row(p.sf, m, K, lane);
-      __syncwarp();
-      continue;
+      return;
     }
-    const uint4 *row_s = bufs + cur * row_chunks;
 
     // sum of squares, numpy pairwise order: leaf j = elements [leaf_len*j, leaf_len*j + leaf_len); lane l
     // owns leaves l, l+32, l+64, l+96; each round's 32 leaves reduce by a butterfly (a balanced tree), and
@@ -653,6 +649,14 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
       }
       if (g < gpr) group(g, swz(2 * g), 0);
     }
+  };
+
+  int cur = 0;
+  for (int64_t m = warp0; m < p.padded; m += nwarps, cur ^= 1, advance()) {
+    fetch(m + nwarps, bufs + (cur ^ 1) * row_chunks);
+    cp_async_wait_1();  // this row's copies (all but the newest group) have landed
+    __syncwarp();
+    row_body(m, bufs + cur * row_chunks);
     __syncwarp();  // every lane is done with this buffer before it is refilled
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
