@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
     ap.add_argument("--workload", choices=["edit_1k", "serving", "headshard"], default="edit_1k",
                     help="edit_1k: the 1K-edit turn (default, the headline); serving: 64 mixed 1K/2K sessions")
-    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu"], default=None,
+    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu", "short_rows"], default=None,
                     help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
     return ap.parse_args()
 
@@ -932,6 +932,13 @@ def profile_case(kind: str) -> None:
         slots = pool.alloc(n)
         buf = torch.randn(layers, 2, n, H, D, device=device).bfloat16()
         fn = (lambda: pool.gather_into(slots, buf)) if kind == "gather" else (lambda: pool.write(slots, buf))
+    elif kind == "short_rows":  # 768 B rows (3 of 24 heads: an 8-way head-sharded pool), 60 layers, 2K prefix
+        hl, n = 3, 16896
+        pool = PagedKVPool("dit-shard", L, hl, D, 24 << 30, torch.bfloat16, device, page_size=PAGE)
+        pool.index.shuffle_free(5)
+        slots = pool.alloc(n)
+        buf = torch.empty(L, 2, n, hl, D, dtype=torch.bfloat16, device=device)
+        fn = lambda: pool.gather_into(slots, buf)  # noqa: E731
     elif kind == "norm":
         T, K = 32768, 3072
         x = torch.randn(1, T, K, dtype=torch.bfloat16, device=device)

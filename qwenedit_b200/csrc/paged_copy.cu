@@ -163,20 +163,20 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
     char *pool_plane = p.pool.plane(plane);
     const char *other_plane =
         kPtrs ? static_cast<const char *>(p.other_ptrs[plane]) : static_cast<const char *>(p.other.plane(plane));
+    // the R rows of the pass are one run on the contiguous side: vector v of the pass is run[v]
+    V *run = reinterpret_cast<V *>(const_cast<char *>(other_plane) + t0 * p.row_bytes);
+    V buf[kRowsUnroll];
+    uint32_t valid = 0u;
     // (row, vector) of vector lane + 32 k of the pass, advanced by 32 per k
     int ri = int(lane / vpr);
     int64_t vec = lane - int64_t(ri) * vpr;
-    V buf[kRowsUnroll];
-    V *dst_at[kRowsUnroll];
 #pragma unroll
     for (int k = 0; k < kRowsUnroll; ++k) {
       const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
-      dst_at[k] = nullptr;
       if (ri < R && slot >= 0) {
-        V *pool_v = reinterpret_cast<V *>(pool_plane + slot * p.row_bytes) + vec;
-        const V *other_v = reinterpret_cast<const V *>(other_plane + (t0 + ri) * p.row_bytes) + vec;
-        buf[k] = load_v<V>(kGather ? pool_v : other_v);
-        dst_at[k] = kGather ? const_cast<V *>(other_v) : pool_v;
+        valid |= 1u << k;
+        buf[k] = kGather ? load_v<V>(reinterpret_cast<const V *>(pool_plane + slot * p.row_bytes) + vec)
+                         : load_v<V>(run + lane + 32 * k);
       }
       vec += 32;
       while (vec >= vpr) {
@@ -184,9 +184,23 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
         ++ri;
       }
     }
+    if (kGather) {
 #pragma unroll
-    for (int k = 0; k < kRowsUnroll; ++k) {
-      if (dst_at[k]) store_v<V>(dst_at[k], buf[k]);
+      for (int k = 0; k < kRowsUnroll; ++k)
+        if (valid & (1u << k)) store_v<V>(run + lane + 32 * k, buf[k]);
+    } else {  // walk the pass again for the pool rows
+      ri = int(lane / vpr);
+      vec = lane - int64_t(ri) * vpr;
+#pragma unroll
+      for (int k = 0; k < kRowsUnroll; ++k) {
+        const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
+        if (valid & (1u << k)) store_v<V>(reinterpret_cast<V *>(pool_plane + slot * p.row_bytes) + vec, buf[k]);
+        vec += 32;
+        while (vec >= vpr) {
+          vec -= vpr;
+          ++ri;
+        }
+      }
     }
   }
 }
