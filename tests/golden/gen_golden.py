@@ -16,6 +16,8 @@ the tests use everywhere else. What it runs:
 * paged  — multi_turn/cache/paged.py's own ``gather`` / ``write`` methods (pure torch: a view or
            index_select, index_copy_) on a seeded pool, with the sglang imports stubbed (the tree is not used)
            -> paged.npz
+* latents — multi_turn/pipeline/masking.py's ``MaskState.blend`` and multi_turn/state.py's ``stored_latents``
+           crop, imported as is, on seeded latents -> latents.npz
 """
 
 from __future__ import annotations
@@ -248,6 +250,53 @@ def gen_paged(out: Path):
     (out / "paged.json").write_text(json.dumps(digests, indent=1))
 
 
+# per-step latent ops: the reference's own MaskState.blend (pipeline/masking.py:82-89) and stored_latents crop
+# (state.py:52-62), run on CPU torch (the same op-by-op fp32-then-round arithmetic as on the GPU)
+LATENT_CASES = [
+    dict(name="blend_bf16", dtype="bfloat16", B=2, N=256, C=16, sigma=0.37, sigma_kind="tensor", seed=501),
+    dict(name="blend_fp16_float_sigma", dtype="float16", B=1, N=512, C=8, sigma=0.618, sigma_kind="float", seed=502),
+    dict(name="blend_fp32_sigma0", dtype="float32", B=2, N=128, C=4, sigma=0.0, sigma_kind="tensor", seed=503),
+    dict(name="blend_bf16_sigma1", dtype="bfloat16", B=1, N=64, C=64, sigma=1.0, sigma_kind="tensor", seed=504),
+]
+CROP_CASES = [dict(name="crop_bf16", h=16, w=24, C=16, box=(3, 2, 17, 9), seed=601),
+              dict(name="crop_fp32_full_width", h=8, w=8, C=4, box=(0, 1, 8, 5), seed=602)]
+
+
+def latent_inputs(case):
+    dt = getattr(torch, case["dtype"])
+    B, N, C, seed = case["B"], case["N"], case["C"], case["seed"]
+    lat = inputs.f32(seed, (B, N, C)).to(dt)
+    x0 = inputs.f32(seed + 1, (1, N, C)).to(dt)
+    eps = inputs.f32(seed + 2, (B, N, C)).to(dt)
+    m = torch.from_numpy(inputs.uniforms(seed + 3, N).astype(np.float32)).view(1, N, 1)
+    m[:, : N // 4] = 0.0
+    m[:, N // 4 : N // 2] = 1.0
+    return lat, x0, eps, m
+
+
+def gen_latents(out: Path) -> None:
+    from multi_turn import state as ref_state
+    from multi_turn.pipeline.masking import MaskState
+
+    arrays = {}
+    for case in LATENT_CASES:
+        lat, x0, eps, m = latent_inputs(case)
+        sigma = torch.tensor(case["sigma"]) if case["sigma_kind"] == "tensor" else case["sigma"]
+        got = MaskState(x0=x0, editable=m, eps=eps).blend(lat, sigma)
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        arrays[case["name"]] = got.contiguous().view(bits).numpy()
+    for case in CROP_CASES:
+        h, w, C = case["h"], case["w"], case["C"]
+        dt = torch.bfloat16 if "bf16" in case["name"] else torch.float32
+        lat = inputs.f32(case["seed"], (1, h * w, C)).to(dt)
+        ref_state.OUTPUT_LATENTS.put(case["name"], lat)
+        ref_state.OUTPUT_GRID[case["name"]] = (h, w)
+        got = ref_state.stored_latents(case["name"], case["box"])
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        arrays[case["name"]] = got.contiguous().view(bits).numpy()
+    np.savez_compressed(out / "latents.npz", **arrays)
+
+
 def hash_seed(name: str) -> int:
     return int(hashlib.sha256(name.encode()).hexdigest()[:8], 16)
 
@@ -255,10 +304,10 @@ def hash_seed(name: str) -> int:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["keys", "nvfp4", "paged"], default=None)
+    ap.add_argument("--only", choices=["keys", "nvfp4", "paged", "latents"], default=None)
     args = ap.parse_args()
     import_reference(Path(args.reference))
-    for part, fn in (("keys", gen_keys), ("paged", gen_paged), ("nvfp4", gen_nvfp4)):
+    for part, fn in (("keys", gen_keys), ("paged", gen_paged), ("nvfp4", gen_nvfp4), ("latents", gen_latents)):
         if args.only in (None, part):
             fn(HERE)
             print("wrote", part)

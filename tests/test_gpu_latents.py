@@ -61,3 +61,38 @@ def test_bad_boxes_raise():
         latents.crop(base, (4, 4), (0, 0, 5, 1))
     with pytest.raises(ValueError):
         latents.compose(base, (4, 4), torch.zeros(1, 1, 4, device=DEV), (2, 2, 2, 3))
+
+
+def test_kernels_match_reference_golden():
+    """The kernels against the reference's own MaskState.blend / stored_latents outputs (latents.npz, made by
+    tests/golden/gen_golden.py from the reference code on CPU)."""
+    from pathlib import Path
+
+    import numpy as np
+
+    from tests.golden.gen_golden import CROP_CASES, LATENT_CASES, latent_inputs
+    from tests.golden import inputs
+
+    gold = np.load(Path(__file__).resolve().parent / "golden" / "latents.npz")
+    for case in LATENT_CASES:
+        lat, x0, eps, m = (t.to(DEV) for t in latent_inputs(case))
+        sigma = (torch.tensor(case["sigma"], device=DEV) if case["sigma_kind"] == "tensor" else case["sigma"])
+        got = latents.mask_blend(lat, x0, eps, m, sigma).cpu()
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        np.testing.assert_array_equal(got.view(bits).numpy(), gold[case["name"]], err_msg=case["name"])
+    for case in CROP_CASES:
+        dt = torch.bfloat16 if "bf16" in case["name"] else torch.float32
+        lat = inputs.f32(case["seed"], (1, case["h"] * case["w"], case["C"])).to(dt).to(DEV)
+        got = latents.crop(lat, (case["h"], case["w"]), case["box"]).cpu()
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        np.testing.assert_array_equal(got.view(bits).numpy(), gold[case["name"]], err_msg=case["name"])
+
+
+def test_reference_blend_keeps_source_outside_at_sigma_zero():
+    """tests/test_core.py:59-63 of the reference, on the kernel."""
+    g = torch.Generator().manual_seed(3)
+    x0 = torch.randn(1, 4, 3, generator=g).to(DEV)
+    eps = torch.randn(1, 4, 3, generator=g).to(DEV)
+    out = latents.mask_blend(torch.zeros(1, 4, 3, device=DEV), x0, eps,
+                             torch.tensor([1.0, 0, 0, 1], device=DEV).view(1, 4, 1), 0.0)
+    assert torch.equal(out[0, 1], x0[0, 1]) and torch.equal(out[0, 0], torch.zeros(3, device=DEV))

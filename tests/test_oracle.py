@@ -108,3 +108,26 @@ def test_reference_pool_data_movement_matches_golden(name):
     assert sha(got) == digests["gather"]
     assert sha(pool.kv) == digests["write"]
     assert pool.stats.gathers == 1 and pool.stats.contiguous_views == 1
+
+
+def test_latent_oracle_matches_reference_golden():
+    """oracle/latents_ref.py against the reference's own MaskState.blend and stored_latents crop
+    (tests/golden/gen_golden.py, latents.npz): bit-exact on CPU."""
+    import torch
+
+    from oracle import latents_ref
+    from tests.golden.gen_golden import CROP_CASES, LATENT_CASES, latent_inputs
+
+    gold = np.load(Path(__file__).resolve().parent / "golden" / "latents.npz")
+    for case in LATENT_CASES:
+        lat, x0, eps, m = latent_inputs(case)
+        sigma = torch.tensor(case["sigma"]) if case["sigma_kind"] == "tensor" else case["sigma"]
+        got = latents_ref.blend(lat, x0, eps, m, sigma)
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        np.testing.assert_array_equal(got.contiguous().view(bits).numpy(), gold[case["name"]])
+    for case in CROP_CASES:
+        dt = torch.bfloat16 if "bf16" in case["name"] else torch.float32
+        lat = inputs.f32(case["seed"], (1, case["h"] * case["w"], case["C"])).to(dt)
+        got = latents_ref.crop(lat, (case["h"], case["w"]), case["box"])
+        bits = torch.int32 if got.dtype == torch.float32 else torch.int16
+        np.testing.assert_array_equal(got.contiguous().view(bits).numpy(), gold[case["name"]])
