@@ -15,7 +15,8 @@ def test_lru_forgets_least_recently_used():
     assert lru.get("b") is None and lru.get("a") == 1 and lru.get("c") == 3
     lru.put("a", 4)  # re-put refreshes and replaces
     lru.put("d", 5)
-    assert lru.get("c") is None and lru.get("a") == 4 and list(lru.items) == ["a", "d"]
+    assert list(lru.items) == ["a", "d"]
+    assert lru.get("c") is None and lru.get("a") == 4 and list(lru.items) == ["d", "a"]
 
 
 def test_stored_latents_crop_rules():
