@@ -111,15 +111,51 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+_fns: dict = {}
+
+
 def call(name: str, *args) -> None:
     """Call entry point `name`; map a non-zero status to ValueError (bad argument) or QEError."""
-    handle = lib()
-    status = getattr(handle, name)(*args)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = _fns[name] = getattr(lib(), name)
+    status = fn(*args)
     if status != QE_OK:
-        message = f"{name}: {handle.qe_last_error().decode(errors='replace')}"
+        message = f"{name}: {lib().qe_last_error().decode(errors='replace')}"
         if status == QE_ERR_INVALID:
             raise ValueError(message)
         raise QEError(status, message)
+
+
+class on_device:
+    """``torch.cuda.device(d)`` only when `d` is not already the current device (entering it costs a switch)."""
+
+    __slots__ = ("index", "ctx")
+
+    def __init__(self, device):
+        self.index = device if isinstance(device, int) else device.index
+        self.ctx = None
+
+    def __enter__(self):
+        import torch
+
+        if self.index is not None and self.index != torch.cuda.current_device():
+            self.ctx = torch.cuda.device(self.index)
+            self.ctx.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
+        return False
+
+
+def stream_of(device) -> int:
+    """Raw handle of torch's current CUDA stream on `device` (an int: a torch.device or its index)."""
+    import torch
+
+    index = device if isinstance(device, int) else device.index
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def version() -> str:
@@ -135,5 +171,5 @@ def ptr64(array) -> "ctypes._Pointer":
     return array.ctypes.data_as(_P64)
 
 
-__all__ = ["LIB_PATH", "QEError", "Planes", "SIGNATURES", "call", "lib", "planes", "ptr64", "version",
-           "c_uint8"]
+__all__ = ["LIB_PATH", "QEError", "Planes", "SIGNATURES", "call", "lib", "on_device", "planes", "ptr64",
+           "stream_of", "version", "c_uint8"]

@@ -39,10 +39,12 @@ def _buffers(x: torch.Tensor, k: int):
 
 
 def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
-    if t.device.type != "cuda":
+    if not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor (the NVFP4 kernels have no CPU path)")
     if t.dtype != torch.bfloat16:
         raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+
+
 
 
 def _gs(gs: torch.Tensor, device) -> torch.Tensor:
@@ -130,9 +132,9 @@ def norm_scale_fp4(x, norm, noisy, clean, noise_mask, gs, shift=None, shift_clea
     a = _norm_args(x, norm, noisy, clean, noise_mask, shift, shift_clean)
     _, _, q, sf = _buffers(x, a.k)
     gs = _gs(gs, x.device)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x.device):
         _lib.call("qe_norm_scale_fp4", *a.pointers(x), gs.data_ptr(), a.m, a.s, a.k, a.stride, float(norm.eps),
-                  q.data_ptr(), sf.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+                  q.data_ptr(), sf.data_ptr(), _lib.stream_of(x.device))
     return Quantized(q, sf, x.shape)
 
 
@@ -151,9 +153,9 @@ def norm_scale_amax(x, norm, noisy, clean, noise_mask, shift=None, shift_clean=N
     bf16 pass ``_norm_scale(...)`` + ``.float().abs().amax()`` (fibo/fp4.py:128-134, pipeline/fp4.py:33-35)."""
     a = _norm_args(x, norm, noisy, clean, noise_mask, shift, shift_clean)
     amax = torch.empty(1, dtype=torch.float32, device=x.device)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x.device):
         _lib.call("qe_norm_scale_amax", *a.pointers(x), a.m, a.s, a.k, a.stride, float(norm.eps), amax.data_ptr(),
-                  torch.cuda.current_stream(x.device).cuda_stream)
+                  _lib.stream_of(x.device))
     return amax
 
 
@@ -162,6 +164,10 @@ _silu_tables: dict[int, torch.Tensor] = {}
 
 def silu_table(device) -> torch.Tensor:
     """Per-device table of bf16(silu(g)) for all 65,536 bf16 g (128 KiB), built once by ``qe_silu_table_init``."""
+    if isinstance(device, torch.device) and device.index is not None:
+        table = _silu_tables.get(device.index)
+        if table is not None:
+            return table
     device = torch.device(device)
     index = device.index if device.index is not None else torch.cuda.current_device()
     table = _silu_tables.get(index)
@@ -193,9 +199,9 @@ def silu_mul_fp4(gate, value, gs, block=1024) -> Quantized:
     m, k, table = _silu_args(gate, value)
     _, _, q, sf = _buffers(gate, k)
     gs = _gs(gs, gate.device)
-    with torch.cuda.device(gate.device):
+    with _lib.on_device(gate.device):
         _lib.call("qe_silu_mul_fp4", gate.data_ptr(), value.data_ptr(), gs.data_ptr(), m, k, q.data_ptr(),
-                  sf.data_ptr(), table.data_ptr(), torch.cuda.current_stream(gate.device).cuda_stream)
+                  sf.data_ptr(), table.data_ptr(), _lib.stream_of(gate.device))
     return Quantized(q, sf, gate.shape)
 
 
@@ -204,7 +210,7 @@ def silu_mul_amax(gate, value) -> torch.Tensor:
     tensor, in one launch with no bf16 product written (pipeline/fp4.py:33-35)."""
     m, k, table = _silu_args(gate, value)
     amax = torch.empty(1, dtype=torch.float32, device=gate.device)
-    with torch.cuda.device(gate.device):
+    with _lib.on_device(gate.device):
         _lib.call("qe_silu_mul_amax", gate.data_ptr(), value.data_ptr(), m, k, table.data_ptr(), amax.data_ptr(),
-                  torch.cuda.current_stream(gate.device).cuda_stream)
+                  _lib.stream_of(gate.device))
     return amax

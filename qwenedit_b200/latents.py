@@ -20,7 +20,7 @@ _CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 
 def _code(t: torch.Tensor, name: str) -> int:
-    if t.device.type != "cuda":
+    if not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor (the latent kernels have no CPU path)")
     if t.dtype not in _CODES:
         raise TypeError(f"{name}: dtype {t.dtype} not supported (float32, bfloat16, float16)")
@@ -36,7 +36,7 @@ def _batch_stride(t: torch.Tensor, B: int, name: str) -> int:
 
 
 def _stream(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    return _lib.stream_of(device)
 
 
 def mask_blend(latents: torch.Tensor, x0: torch.Tensor, eps: torch.Tensor, editable: torch.Tensor,
@@ -72,7 +72,7 @@ def mask_blend(latents: torch.Tensor, x0: torch.Tensor, eps: torch.Tensor, edita
         sig = torch.tensor([s, 1.0 - s], dtype=torch.float32).to(dev)
         scode = 3
     out = torch.empty_like(latents)
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         _lib.call("qe_mask_blend", latents.data_ptr(), x0.data_ptr(), eps.data_ptr(), editable.data_ptr(),
                   sig.data_ptr(), out.data_ptr(), B, N, C, _batch_stride(x0, B, "x0"), _batch_stride(eps, B, "eps"),
                   _batch_stride(editable, B, "editable"), int(editable.shape[2]), dtype, mcode, scode, _stream(dev))
@@ -103,7 +103,7 @@ def compose(base: torch.Tensor, base_grid, crop_latents: torch.Tensor, box) -> t
     if crop.numel() != (y1 - y0) * (x1 - x0) * C:
         raise ValueError("crop latents do not match the box")
     out = torch.empty(1, h * w, C, dtype=base.dtype, device=base.device)
-    with torch.cuda.device(base.device):
+    with _lib.on_device(base.device):
         _lib.call("qe_latent_compose", base.data_ptr(), crop.data_ptr(), out.data_ptr(), h, w, C * base.element_size(),
                   x0, y0, x1, y1, _stream(base.device))
     return out
@@ -118,7 +118,7 @@ def crop(latents: torch.Tensor, grid, box) -> torch.Tensor:
     if latents.numel() != h * w * C or not latents.is_contiguous():
         raise ValueError("latents must be contiguous [1, h*w, C]")
     out = torch.empty(1, (y1 - y0) * (x1 - x0), C, dtype=latents.dtype, device=latents.device)
-    with torch.cuda.device(latents.device):
+    with _lib.on_device(latents.device):
         _lib.call("qe_latent_crop", latents.data_ptr(), out.data_ptr(), h, w, C * latents.element_size(), x0, y0, x1,
                   y1, _stream(latents.device))
     return out

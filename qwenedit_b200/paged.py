@@ -273,7 +273,7 @@ class PagedKVPool:
         return self.heads * self.head_dim * t.element_size()
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self.device).cuda_stream
+        return _lib.stream_of(self.device)
 
     def _block_table(self, indices: torch.Tensor, host: np.ndarray) -> torch.Tensor | None:
         """Device int32 page table when the slots are whole-page runs (page mode), else None."""
@@ -346,7 +346,7 @@ class PagedKVPool:
             oth = _lib.planes(out.data_ptr(), out.stride(0) * e, out.stride(1) * e, 2)
             slots = indices if indices.dtype == torch.int64 else indices.to(torch.int64)
             slots = slots.contiguous()
-            with torch.cuda.device(self.device):
+            with _lib.on_device(self.device):
                 _lib.call("qe_gather_slots_heads", pool, self.rows, oth, 2 * self.layers, self._row_bytes(self.kv),
                           self.head_dim * e, out.stride(2) * e, out.stride(3) * e, slots.data_ptr(), n,
                           self._err.data_ptr(), self._stream())
@@ -394,7 +394,7 @@ class PagedKVPool:
         e = self.kv.element_size()
         pool = _lib.planes(self.kv.data_ptr(), self.kv.stride(0) * e, self.kv.stride(1) * e, 2)
         slots = indices if indices.dtype == torch.int64 else indices.to(torch.int64)
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _lib.call("qe_append_slots_ptrs", pool, self.rows, table.data_ptr(), 2 * self.layers, row,
                       slots.data_ptr(), n, self._err.data_ptr(), self._stream())
         # keep the sources and the pointer table alive until the launch has consumed them
@@ -439,7 +439,7 @@ class PagedKVPool:
         oth = _lib.planes(other.data_ptr(), other.stride(0) * e, other.stride(1) * e, 2)
         n = indices.numel()
         bt = self._block_table(indices, host) if host is not None else None
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             if bt is not None:
                 _lib.call(f"qe_{kind}_pages", pool, self.rows, oth, n_planes, row, bt.data_ptr(), self.page_size, n,
                           self._err.data_ptr(), self._stream())
@@ -456,7 +456,7 @@ class PagedKVPool:
         oth = _lib.planes(other.data_ptr(), 0, 0, 1)
         slots = indices if indices.dtype == torch.int64 else indices.to(torch.int64)
         slots = slots.contiguous()
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _lib.call(f"qe_{kind}_slots", pool, self.rows, oth, 1, row, slots.data_ptr(), indices.numel(),
                       self._err.data_ptr(), self._stream())
 
