@@ -68,7 +68,7 @@ typedef struct qe_planes {
 int qe_gather_slots(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
                     const int64_t *slots, int64_t n_tokens, int32_t *err_flag, void *stream);
 
-/* gather through a page table (page_size tokens per page; BASELINE perf mode). */
+/* gather through a page table (page_size tokens per page; the paged mode the 1K / 2K edit benchmark uses). */
 int qe_gather_pages(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
                     const int32_t *block_table, int32_t page_size, int64_t n_tokens, int32_t *err_flag,
                     void *stream);
@@ -136,7 +136,7 @@ int qe_set_paged_copy_mode(int32_t mode);
  *   shared by every batch);
  *   mask: uint8 [S] or null (null: every token uses `noisy`); clean may be null when mask is null;
  *   shift / shift_clean: optional bf16 adaLN shift rows with the same layout and mask select
- *   (BASELINE's x*(1+scale)+shift; the reference has no shift). */
+ *   (the adaLN form x*(1+scale)+shift of the benchmark; the reference has no shift). */
 int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const void *clean, const uint8_t *mask,
                       const void *shift, const void *shift_clean, const float *gs, int64_t M, int64_t S,
                       int64_t K, int64_t mod_stride, float eps, uint8_t *q, uint8_t *sf, void *stream);

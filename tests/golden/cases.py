@@ -8,7 +8,7 @@ from tests.golden import inputs
 
 # RMSNorm + adaLN -> NVFP4. "fibo_mask" mirrors the reference GPU test's shape family (tests/test_fibo_fp4.py:41-49:
 # x*3, weight U+0.5, mods [B, 4K]*0.3 with noisy/clean column slices, token mask, partial 128-row tile);
-# "c4" the BASELINE NVFP4 config family (eps 1e-6, w = 1 + 0.02 N, scale 0.1 N, B = 1).
+# "c4" the benchmark NVFP4 shape family (eps 1e-6, w = 1 + 0.02 N, scale 0.1 N, B = 1).
 NORM_CASES = [
     dict(name="norm_fibo_mask", B=2, S=75, K=3584, eps=1e-5, x_scale=3.0, w_kind="uniform", mod_scale=0.3,
          mask=(20, 60), seed=11),
@@ -19,7 +19,7 @@ NORM_CASES = [
 ]
 
 # SiLU * mul -> NVFP4: Fibo's K=9536 (partial last 1024-column block, tests/test_fibo_fp4.py:53-58) and
-# BASELINE's 12288.
+# the benchmark's 12288.
 SILU_CASES = [
     dict(name="silu_fibo", M=40, K=9536, seed=41),
     dict(name="silu_c4", M=24, K=12288, seed=51),

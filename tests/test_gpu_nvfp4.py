@@ -1,5 +1,5 @@
 """Fused NVFP4 kernels on the GPU: bit-exact against the reference kernels' golden outputs
-(multi_turn/fibo/fp4.py run by tests/golden/gen_golden.py) and against the C oracle over the BASELINE NVFP4
+(multi_turn/fibo/fp4.py run by tests/golden/gen_golden.py) and against the C oracle over the benchmark NVFP4
 shapes, the reference test's shapes (tests/test_fibo_fp4.py:39-58) and edge cases.
 
 Tolerance (stated by the build's spec for NVFP4): bit-exact codes and scales, or <= 1 code step on <= 1e-4 of
@@ -87,7 +87,7 @@ def table_mode(request):
 @pytest.mark.parametrize("T", [4096, 16384])
 @pytest.mark.parametrize("shift", [False, True])
 def test_norm_scale_baseline_shapes(T, shift, table_mode):
-    """BASELINE NVFP4: x [1, T, 3072] ~N(0,1), eps 1e-6, w ~ 1 + 0.02 N, scale/shift ~ 0.1 N."""
+    """Benchmark NVFP4 shapes: x [1, T, 3072] ~N(0,1), eps 1e-6, w ~ 1 + 0.02 N, scale/shift ~ 0.1 N."""
     out, q_ref, sf_ref = _norm_case(1, T, 3072, 1e-6, False, shift, seed=T + shift)
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)

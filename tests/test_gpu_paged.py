@@ -1,5 +1,5 @@
 """Paged K/V gather / append on the GPU against the oracle (the reference's index_select / index_copy_ on CPU),
-bit for bit; the reference's own pool tests (tests/test_paged.py:28-65) replayed on CUDA; the BASELINE CPU
+bit for bit; the reference's own pool tests (tests/test_paged.py:28-65) replayed on CUDA; the CPU
 round-trip config; and size-independent properties at the 1K-edit shapes."""
 
 import numpy as np
@@ -246,7 +246,7 @@ def _randn(seed, shape):
 
 
 def test_cpu_round_trip_config():
-    """BASELINE CPU round trip (4 layers, 24 x 128, fp32 ~N(0,1), page 64, 512 pages; 3 sessions of 4096 image +
+    """The CPU-sized round-trip workload (4 layers, 24 x 128, fp32 ~N(0,1), page 64, 512 pages; 3 sessions of 4096 image +
     256 text tokens; append one 4096-token turn each; gather each session) vs the oracle pool, bit-exact."""
     L, H, D, P = 4, 24, 128, 64
     budget = 512 * P * L * 2 * H * D * 4

@@ -1,4 +1,4 @@
-"""BASELINE's 2K multi-turn config under memory pressure, at full token counts: 8 sessions x 5 turns of a
+"""The 2K multi-turn workload under memory pressure, at full token counts: 8 sessions x 5 turns of a
 16,384 + 512-token DiT prefix in a 24 GiB pool (room for two prefixes), plus 1,024-token prompts in a 4 GiB
 encoder pool. Forced LRU eviction; the native index must make the same decisions as the oracle restatement
 (match lengths, evicted token counts, allocated slots, usage) at every step. Index-only (meta device), CPU."""
