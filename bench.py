@@ -394,6 +394,51 @@ def extras(pool, sess, device):
     out["nvfp4_cpu_baseline"] = nvfp4_cpu()
     out["mask_blend_1k"] = latent_extras(device)
     out["encoder_prompt_1k"] = encoder_extras(device, peak)
+    out["prefix_index_host_latency_1k"] = index_latency()
+    return out
+
+
+def index_latency(turns: int = 40, page: int = PAGE) -> dict:
+    """Host latency of the prefix index per 1K-edit turn (SURVEY-style: reported as latency, not bandwidth):
+    match of the 4,608-token prefix, alloc of the 4,096 new tokens (with LRU eviction once the 24 GiB pool is
+    full), insert of the next prefix, release. The native index (libqeb200) against the oracle's Python
+    restatement of the reference's tree (SGLang RadixCache + allocator), both index-only (no device data)."""
+    from oracle.pool_ref import RefPagedKVPool
+    from qwenedit_b200.paged import PagedKVPool
+
+    budget = POOL_GIB << 30
+    ours = PagedKVPool("idx", L, H, D, budget, torch.bfloat16, "meta", page_size=page)
+    ref = RefPagedKVPool("idx", L, H, D, budget, torch.bfloat16, page_size=page, allocate=False)
+    rng = np.random.default_rng(4)
+    text = rng.integers(1, 1 << 62, size=TEXT)
+    images = [rng.integers(1, 1 << 62, size=IMAGE) for _ in range(turns + 2)]
+    out = {}
+    for name, pool in (("native", ours), ("python_reference_tree", ref)):
+        first = np.concatenate([text, images[0]])
+        s0 = pool.alloc(PREFIX)
+        pool.insert(first, s0, owned_from=0)
+        t = {"match": [], "alloc": [], "insert": [], "release": []}
+        for turn in range(turns):
+            a = time.perf_counter()
+            m = pool.match(np.concatenate([text, images[turn]]))
+            b = time.perf_counter()
+            slots = pool.alloc(APPEND)
+            c = time.perf_counter()
+            host = np.concatenate([np.asarray(m.indices[:TEXT].numpy() if not hasattr(m.indices, "_qe_host")
+                                              else m.indices._qe_host[:TEXT]), np.asarray(
+                slots._qe_host if hasattr(slots, "_qe_host") else slots.numpy())])
+            idx = torch.from_numpy(host.copy())
+            idx._qe_host = idx.numpy()
+            d = time.perf_counter()
+            pool.insert(np.concatenate([text, images[turn + 1]]), idx, owned_from=TEXT)
+            e = time.perf_counter()
+            m.release()
+            f = time.perf_counter()
+            for k, v in (("match", b - a), ("alloc", c - b), ("insert", e - d), ("release", f - e)):
+                t[k].append(v * 1e6)
+        out[name] = {k: round(statistics.median(v), 1) for k, v in t.items()}
+        out[name]["evicted_tokens"] = int(pool.usage()["evicted_tokens"] if hasattr(pool, "usage") else 0)
+    out["unit"] = "us per call (median over turns)"
     return out
 
 
