@@ -407,7 +407,11 @@ struct Index {
     if (page == 1) {
       std::memcpy(out, u, size_t(n) * sizeof(int64_t));
     } else {
-      for (int64_t t = 0; t < n; ++t) out[t] = u[t / page] * page + t % page;
+      int64_t t = 0;
+      for (int64_t i = 0; i < units && t < n; ++i) {
+        const int64_t base = u[i] * page;
+        for (int64_t o = 0; o < page && t < n; ++o) out[t++] = base + o;
+      }
     }
     for (int64_t i = 0; i < units; ++i) unit_free[size_t(u[i])] = 0;
     free_head += size_t(units);
@@ -430,9 +434,14 @@ struct Index {
       release_units.insert(release_units.end(), s, s + n);
       return true;
     }
-    // unique pages, ascending (torch.unique(free_index // page_size))
-    std::vector<int64_t> pages(static_cast<size_t>(n));
-    for (int64_t i = 0; i < n; ++i) pages[size_t(i)] = s[i] >= 0 ? s[i] / page : -1;
+    // unique pages, ascending (torch.unique(free_index // page_size)); the slots of a page come as runs, so
+    // adjacent repeats are dropped first and only the distinct pages are sorted
+    std::vector<int64_t> pages;
+    pages.reserve(static_cast<size_t>(n / page + 2));
+    for (int64_t i = 0; i < n; ++i) {
+      const int64_t p = s[i] >= 0 ? s[i] / page : -1;
+      if (pages.empty() || pages.back() != p) pages.push_back(p);
+    }
     std::sort(pages.begin(), pages.end());
     pages.erase(std::unique(pages.begin(), pages.end()), pages.end());
     if (check) {
