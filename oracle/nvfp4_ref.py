@@ -154,4 +154,3 @@ def global_scale(y: torch.Tensor, headroom: float = 4.0) -> float:
 
 
 __all__ = ["build", "lib", "norm_scale_fp4_ref", "silu_mul_fp4_ref", "bf16_values_norm_scale", "global_scale"]
-_ = (c_uint8,)

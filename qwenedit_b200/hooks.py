@@ -19,7 +19,6 @@ import logging
 import time
 from typing import Callable
 
-import numpy as np
 import torch
 
 from qwenedit_b200 import state
@@ -135,4 +134,3 @@ def encoder_store(pool: PagedKVPool, vids, match: Match | None, kv_new: torch.Te
 
 
 __all__ = ["MTCaches", "set_caches", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store"]
-_ = np
