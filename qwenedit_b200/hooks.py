@@ -133,4 +133,27 @@ def encoder_store(pool: PagedKVPool, vids, match: Match | None, kv_new: torch.Te
     return True
 
 
-__all__ = ["MTCaches", "set_caches", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store"]
+# ---- stored output versions ---------------------------------------------------------------------
+def compose(spec: dict, crop_latents: torch.Tensor, crop_grid: tuple[int, int]) -> bool:
+    """``_compose`` (pipeline/hooks.py:232-247): store, as version ``spec["as"]``, the latents of version
+    ``spec["base"]`` with the cells of ``spec["box"]`` replaced by ``crop_latents`` — one launch
+    (``latents.compose``) instead of clone + slice assignment. Same checks and warnings; returns False when
+    nothing was stored (missing base, or a box that does not match the crop grid)."""
+    from qwenedit_b200 import latents
+
+    base = state.OUTPUT_LATENTS.get(spec.get("base"))
+    base_grid = state.OUTPUT_GRID.get(spec.get("base"))
+    if base is None or base_grid is None:
+        logger.warning("qwenedit_b200: compose base %s missing; the new version has no stored latents",
+                       spec.get("base"))
+        return False
+    x0, y0, x1, y1 = (int(v) for v in spec["box"])
+    if (y1 - y0, x1 - x0) != tuple(crop_grid):
+        logger.warning("qwenedit_b200: compose box %s does not match the crop grid %s", spec["box"], crop_grid)
+        return False
+    state.OUTPUT_LATENTS.put(spec["as"], latents.compose(base, base_grid, crop_latents, (x0, y0, x1, y1)))
+    state.OUTPUT_GRID[spec["as"]] = base_grid
+    return True
+
+
+__all__ = ["MTCaches", "set_caches", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store", "compose"]

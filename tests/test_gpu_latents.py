@@ -96,3 +96,22 @@ def test_reference_blend_keeps_source_outside_at_sigma_zero():
     out = latents.mask_blend(torch.zeros(1, 4, 3, device=DEV), x0, eps,
                              torch.tensor([1.0, 0, 0, 1], device=DEV).view(1, 4, 1), 0.0)
     assert torch.equal(out[0, 1], x0[0, 1]) and torch.equal(out[0, 0], torch.zeros(3, device=DEV))
+
+
+def test_compose_hook_stores_the_new_version():
+    """hooks.compose against the reference's _compose sequence (oracle restatement): the stored version, its
+    grid, and the two refusals (missing base, box not matching the crop grid)."""
+    from qwenedit_b200 import hooks, state
+
+    h, w, C = 12, 16, 16
+    g = torch.Generator().manual_seed(9)
+    base = torch.randn(1, h * w, C, generator=g).bfloat16().to(DEV)
+    piece = torch.randn(1, 4 * 5, C, generator=g).to(DEV)
+    state.OUTPUT_LATENTS.put("v1", base)
+    state.OUTPUT_GRID["v1"] = (h, w)
+    assert hooks.compose({"base": "v1", "as": "v2", "box": (3, 2, 8, 6)}, piece, (4, 5))
+    want = latents_ref.compose(base, (h, w), piece, (3, 2, 8, 6))
+    assert torch.equal(state.OUTPUT_LATENTS.get("v2"), want) and state.OUTPUT_GRID["v2"] == (h, w)
+    assert not hooks.compose({"base": "missing", "as": "v3", "box": (0, 0, 1, 1)}, piece, (1, 1))
+    assert not hooks.compose({"base": "v1", "as": "v3", "box": (0, 0, 2, 2)}, piece, (4, 5))
+    assert state.OUTPUT_LATENTS.get("v3") is None
