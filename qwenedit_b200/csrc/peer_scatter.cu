@@ -149,15 +149,15 @@ int qe_append_scatter(const void *const *peer_pools, int32_t n_peers, qe_planes 
   QE_CHECK_ARG(pool.outer_stride % 16 == 0 && pool.inner_stride % 16 == 0 && src.outer_stride % 16 == 0 &&
                    src.inner_stride % 16 == 0,
                "qe_append_scatter: plane strides must be multiples of 16 bytes");
+  if (n_tokens == 0) return qe::ok();
   QE_CHECK_ARG(src.base && qe::aligned16(src.base), "qe_append_scatter: source must be 16-byte aligned");
-  QE_CHECK_ARG(n_tokens == 0 || slots, "qe_append_scatter: null slots");
+  QE_CHECK_ARG(slots, "qe_append_scatter: null slots");
   qe::ScatterParams p{};
   for (int r = 0; r < n_peers; ++r) {
     QE_CHECK_ARG(peer_pools[r] && qe::aligned16(peer_pools[r]), "qe_append_scatter: peer pool %d null or unaligned",
                  r);
     p.peer[r] = static_cast<char *>(const_cast<void *>(peer_pools[r]));
   }
-  if (n_tokens == 0) return qe::ok();
   p.outer = pool.outer_stride;
   p.inner = pool.inner_stride;
   p.per_outer = pool.planes_inner;
