@@ -143,8 +143,8 @@ int qe_norm_scale_fp4(const void *x, const void *w, const void *noisy, const voi
 
 /* Where qe_norm_scale_fp4 / qe_norm_scale_amax keep the per-column constants (process-wide): 0 = default
  * (tensor memory when K is the specialised width 3072, M >= 12288 rows and they fit 256 TMEM columns, else
- * shared memory or global memory), 1 = never tensor memory. Results are identical either way. No counterpart in the reference;
- * for measurement and tests. */
+ * shared memory or global memory), 1 = never tensor memory, 2 = always global memory (read through L1). Results
+ * are identical in every mode. No counterpart in the reference; for measurement and tests. */
 int qe_set_norm_table_mode(int32_t mode);
 
 /* Where qe_silu_mul_fp4 / qe_silu_mul_amax read the SiLU table from (process-wide): 0 = by size (default),

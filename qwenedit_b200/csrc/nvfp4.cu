@@ -250,6 +250,14 @@ __device__ __forceinline__ uint4 ld16(const uint4 *p) {
   return make_uint4(uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w));
 }
 
+// 32 bytes (one 16-value bf16 group) in one 256-bit streaming load; p must be 32-byte aligned. A warp request
+// then covers 32 whole sectors instead of touching 32 sectors twice, half of each per 16-byte load.
+__device__ __forceinline__ void ld32(const uint4 *p, uint4 &a, uint4 &b) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+               : "l"(p));
+}
+
 // zero the scales of padding row m (rows M .. pad128(M)-1 of the last 128-row tile), 4 bytes per store
 __device__ __forceinline__ void zero_sf_row(uint8_t *sf, int64_t m, int64_t K, int lane) {
   for (int g = lane * 4; g < int(K / 16); g += 128) *reinterpret_cast<uint32_t *>(sf + sf_offset(m, g, K)) = 0u;
@@ -728,7 +736,8 @@ int launch_norm_k(int tab, bool shift, int warps, const NormParams &p, size_t sm
                            : launch_norm_warps<kK, 0, false, kAmax>(warps, p, smem, st));
 }
 
-// 0: per-column constants in TMEM where eligible (default); 1: never TMEM (shared-memory / global tables)
+// 0: per-column constants in TMEM where eligible (default); 1: never TMEM (shared-memory / global tables);
+// 2: always global memory
 std::atomic<int> g_norm_table_mode{0};
 bool tmem_tables_enabled() { return g_norm_table_mode.load(std::memory_order_relaxed) == 0; }
 // Below this many rows the per-CTA TMEM setup (allocation, table writes, fences) costs more than the shared-
@@ -782,6 +791,7 @@ struct SiluParams {
   uint8_t *sf;
   float *amax;  // amax mode: max |y| over the whole tensor (the calibration pre-pass)
   int64_t M, K, padded;
+  int32_t wide;  // gate and value are 32-byte aligned: one 256-bit load per lane and tensor
 };
 
 constexpr int kSiluThreads = 1024;  // one CTA per SM (the table takes 128 KiB of shared memory)
@@ -848,10 +858,15 @@ __global__ void __launch_bounds__(silu_threads(kSched), 1) silu_mul_fp4_kernel(S
   auto load = [&](const Item &it, Data &d) {
     if (valid(it)) {
       const int64_t c = it.row * (p.K >> 3) + 2 * (it.seg * 32 + lane);
-      d.ga = ld16(p.gate + c);
-      d.gb = ld16(p.gate + c + 1);
-      d.va = ld16(p.value + c);
-      d.vb = ld16(p.value + c + 1);
+      if (p.wide) {  // rows are whole 128-byte lines (K % 64 == 0), so every group is 32-byte aligned
+        ld32(p.gate + c, d.ga, d.gb);
+        ld32(p.value + c, d.va, d.vb);
+      } else {
+        d.ga = ld16(p.gate + c);
+        d.gb = ld16(p.gate + c + 1);
+        d.va = ld16(p.value + c);
+        d.vb = ld16(p.value + c + 1);
+      }
     }
   };
   auto compute = [&](const Item &it, const Data &d) {
@@ -1005,6 +1020,7 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   int tab = tables <= 64 * 1024 ? 1 : 0;
   if (K == qe::kFixedK && tmem_cols <= int64_t(qe::kTmemCols) && qe::tmem_tables_enabled() && M >= qe::kTmemMinRows)
     tab = 2;
+  if (qe::g_norm_table_mode.load(std::memory_order_relaxed) == 2) tab = 0;  // constants read from global memory
   int best_warps = 0, best_resident = 0;
   size_t best_smem = 0;
   for (int w : {16, 8, 6, 4, 2}) {
@@ -1058,7 +1074,7 @@ int qe_set_silu_pipeline(int32_t on) {
 }
 
 int qe_set_norm_table_mode(int32_t mode) {
-  if (mode < 0 || mode > 1) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0 or 1");
+  if (mode < 0 || mode > 2) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0, 1 or 2");
   qe::g_norm_table_mode.store(mode, std::memory_order_relaxed);
   return qe::ok();
 }
@@ -1105,6 +1121,7 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.M = M;
   p.K = K;
   p.padded = padded;
+  p.wide = ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(value)) & 31) == 0 ? 1 : 0;
   const int mode = g_silu_table_mode.load(std::memory_order_relaxed);
   const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
   const int sched = g_silu_pipeline.load(std::memory_order_relaxed);

@@ -75,9 +75,9 @@ def _norm_case(B, S, K, eps, masked, shift, seed, x_scale=1.0):
     return out, q_ref, sf_ref
 
 
-@pytest.fixture(params=[0, 1], ids=["tmem_tables", "smem_tables"])
+@pytest.fixture(params=[0, 1, 2], ids=["tmem_tables", "smem_tables", "global_tables"])
 def table_mode(request):
-    """Both homes of the per-column constants (tensor memory where eligible, or shared memory)."""
+    """Every home of the per-column constants: tensor memory where eligible, shared memory, global memory."""
     from qwenedit_b200 import _lib
     _lib.call("qe_set_norm_table_mode", request.param)
     yield request.param
@@ -133,6 +133,30 @@ def test_silu_mul_shapes(M, K, silu_mode):
     out = silu_mul_fp4(gate.to(DEV), value.to(DEV), _gs(gs))
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@pytest.mark.parametrize("gate_off,value_off", [(8, 8), (0, 8), (8, 0)])
+def test_silu_mul_16_byte_aligned_inputs(gate_off, value_off):
+    """Contiguous inputs that start 16 bytes past a 32-byte boundary (views into a larger buffer) take the
+    16-byte loads instead of the 256-bit ones; codes, scales and amax are the same."""
+    M, K = 300, 1024
+    gate = inputs.bf16(41, (M, K))
+    value = inputs.bf16(42, (M, K))
+    gs = nvfp4_ref.global_scale(_oracle_silu_y(gate, value))
+    q_ref, sf_ref = nvfp4_ref.silu_mul_fp4_ref(gate, value, gs)
+
+    def placed(t, off):  # t's values in a fresh buffer, starting `off` bf16 elements in
+        buf = torch.zeros(t.numel() + 16, dtype=torch.bfloat16, device=DEV)
+        view = buf[off:off + t.numel()].view(t.shape)
+        view.copy_(t.to(DEV))
+        assert view.data_ptr() % 32 == 2 * off % 32
+        return view
+
+    g, v = placed(gate, gate_off), placed(value, value_off)
+    out = silu_mul_fp4(g, v, _gs(gs))
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+    assert silu_mul_amax(g, v).item() == _oracle_silu_y(gate, value).float().abs().max().item()
 
 
 def test_extreme_values_saturate_like_the_oracle():
