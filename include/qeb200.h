@@ -100,7 +100,9 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
  * cudaGetSymbolAddress, so make that first call before any stream capture. Every call rewrites the table's
  * first n_planes entries on `stream` and the kernel reads them from there: calls whose work can overlap on the
  * GPU (different streams) race on the shared table; issue them on one stream. Allocates nothing: no cudaMalloc,
- * cudaFree or allocating library call; the host array may be reused once the call returns. */
+ * cudaFree or allocating library call. The host array is copied with cudaMemcpyAsync: pageable memory may be
+ * reused once the call returns, pinned memory once `stream` has passed the call. Null source pointers are
+ * rejected; the vector width follows the least-aligned source pointer. */
 int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs_host,
                                  int32_t n_planes, int64_t row_bytes, const int64_t *slots, int64_t n_tokens,
                                  int32_t *err_flag, void *stream);
@@ -116,9 +118,11 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
                           int64_t n_tokens, int32_t *err_flag, void *stream);
 
 /* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel (rows of at
- * most 1 KiB are moved several per warp pass), 2 = TMA bulk-copy pipeline (cp.async.bulk through
- * shared memory; 16-byte aligned rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per
- * warp pass whatever the row size. No counterpart in the reference; for measurement and tuning. */
+ * most 1 KiB are moved several per warp pass; rows above 1 KiB on 32-byte aligned planes move in 256-bit
+ * vectors, else 16-byte ones), 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned
+ * rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per warp pass whatever the row
+ * size, 4 = the warp kernel with 16-byte vectors only. No counterpart in the reference; for measurement and
+ * tuning. */
 int qe_set_paged_copy_mode(int32_t mode);
 
 /* ---- fused NVFP4 activation quantisers (device) ---------------------------------------------

@@ -60,6 +60,11 @@ struct CopyParams {
 
 enum { kSlots = 0, kPages = 1 };
 
+// 32 bytes: one 256-bit load / store per lane (sm_100), so a warp request covers 1 KiB
+struct alignas(32) Vec32 {
+  uint32_t w[8];
+};
+
 template <typename V>
 __device__ __forceinline__ V load_v(const V *p) {
   return *p;
@@ -68,6 +73,15 @@ template <>
 __device__ __forceinline__ int4 load_v<int4>(const int4 *p) {
   return ld_stream(p);
 }
+template <>
+__device__ __forceinline__ Vec32 load_v<Vec32>(const Vec32 *p) {
+  Vec32 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]), "=r"(v.w[6]),
+                 "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
 template <typename V>
 __device__ __forceinline__ void store_v(V *p, V v) {
   *p = v;
@@ -75,6 +89,12 @@ __device__ __forceinline__ void store_v(V *p, V v) {
 template <>
 __device__ __forceinline__ void store_v<int4>(int4 *p, int4 v) {
   st_stream(p, v);
+}
+template <>
+__device__ __forceinline__ void store_v<Vec32>(Vec32 *p, Vec32 v) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+               "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+               : "memory");
 }
 
 // kUnroll vectors per lane are loaded before any is stored: 16 for rows of 6 KiB and more (a whole DiT row in
@@ -489,7 +509,9 @@ int bulk_launch_check(const CopyParams &p, int align) {
   return 1;
 }
 
-int g_copy_mode = 0;  // 0 auto, 1 warp LDG/STG, 2 TMA bulk, 3 warp LDG/STG with one row per warp pass
+// 0 auto, 1 warp LDG/STG, 2 TMA bulk, 3 warp LDG/STG with one row per warp pass, 4 warp LDG/STG with 16-byte
+// vectors only
+int g_copy_mode = 0;
 
 template <int kMode, bool kGather, bool kPtrs>
 int launch_bulk(const CopyParams &p, cudaStream_t stream) {
@@ -575,6 +597,10 @@ bool planes_aligned(const qe_planes &pl, int a) {
 template <int kMode, bool kGather, bool kPtrs>
 int launch(const CopyParams &p, int align, cudaStream_t stream) {
   if (g_copy_mode == 2 && bulk_launch_check(p, align)) return launch_bulk<kMode, kGather, kPtrs>(p, stream);
+  // rows above 1 KiB (one row per warp pass) on 32-byte aligned planes: 256-bit vectors, 8 per lane in flight
+  // (the same bytes as 16 of 16 bytes, half the instructions and L1 requests)
+  if (align >= 32 && g_copy_mode != 4 && (p.row_bytes > 1024 || g_copy_mode == 3))
+    return launch_unrolled<Vec32, kMode, kGather, kPtrs, 8>(p, stream);
   if (align >= 16) return launch_typed<int4, kMode, kGather, kPtrs>(p, stream);
   if (align >= 4) return launch_typed<uint32_t, kMode, kGather, kPtrs>(p, stream);
   return launch_typed<uint8_t, kMode, kGather, kPtrs>(p, stream);
@@ -599,9 +625,9 @@ int common_checks(const char *fn, const qe_planes &pool, int64_t pool_rows, int3
   return QE_OK;
 }
 
-// Largest vector width (16, 4 or 1 bytes) every address of the copy is aligned to.
+// Largest vector width (32, 16, 4 or 1 bytes) every address of the copy is aligned to.
 int align_of(const qe_planes &a, const qe_planes *b, int64_t row_bytes) {
-  for (int w : {16, 4}) {
+  for (int w : {32, 16, 4}) {
     if (row_bytes % w == 0 && planes_aligned(a, w) && (!b || planes_aligned(*b, w))) return w;
   }
   return 1;
@@ -713,8 +739,9 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
   p.n_planes = n_planes;
   p.err = err_flag;
   // Source pointers are only known on the device; the Python side checks each one for 16-byte
-  // alignment before uploading the array, so the width follows the pool and the row size.
-  s = qe::launch<qe::kSlots, false, true>(p, qe::align_of(pool, nullptr, row_bytes), static_cast<cudaStream_t>(stream));
+  // alignment before uploading the array, so the width follows the pool and the row size, up to 16 bytes.
+  s = qe::launch<qe::kSlots, false, true>(p, std::min(16, qe::align_of(pool, nullptr, row_bytes)),
+                                          static_cast<cudaStream_t>(stream));
   return s ? s : qe::ok();
 }
 
@@ -754,7 +781,7 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
 }
 
 int qe_set_paged_copy_mode(int32_t mode) {
-  if (mode < 0 || mode > 3) return fail(QE_ERR_INVALID, "qe_set_paged_copy_mode: mode must be 0, 1, 2 or 3");
+  if (mode < 0 || mode > 4) return fail(QE_ERR_INVALID, "qe_set_paged_copy_mode: mode must be 0, 1, 2, 3 or 4");
   qe::g_copy_mode = mode;
   return qe::ok();
 }
@@ -804,6 +831,13 @@ extern "C" int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, c
                 qe::kStaticMaxPlanes);
   if (n_planes == 0 || n_tokens == 0) return qe::ok();
   if (!src_ptrs_host || !slots) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: null source pointers or slots");
+  // the vector width also follows the source pointers, which are known here on the host
+  int align = qe::align_of(pool, nullptr, row_bytes);
+  for (int32_t i = 0; i < n_planes; ++i) {
+    if (!src_ptrs_host[i]) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: null source pointer %d", i);
+    while (align > 1 && (reinterpret_cast<uintptr_t>(src_ptrs_host[i]) % align) != 0)
+      align = align == 32 ? 16 : align == 16 ? 4 : 1;
+  }
   const void *const *table = nullptr;
   s = qe::static_ptr_table(&table);
   if (s) return s;
@@ -823,6 +857,6 @@ extern "C" int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, c
   p.slots = slots;
   p.n_planes = n_planes;
   p.err = err_flag;
-  s = qe::launch<qe::kSlots, false, true>(p, qe::align_of(pool, nullptr, row_bytes), st);
+  s = qe::launch<qe::kSlots, false, true>(p, align, st);
   return s ? s : qe::ok();
 }

@@ -14,10 +14,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-@pytest.fixture(autouse=True, params=["warp", "warp_row", "bulk"])
+@pytest.fixture(autouse=True, params=["warp", "warp_row", "warp16", "bulk"])
 def copy_kernel(request):
-    """Run every test with every paged-copy kernel (vectorised warp copy, several short rows per warp pass or one
-    row per pass, TMA bulk pipeline)."""
+    """Run every test with every paged-copy kernel (vectorised warp copy with 256-bit vectors where aligned,
+    several short rows per warp pass or one row per pass, 16-byte vectors only, TMA bulk pipeline)."""
     from qwenedit_b200.paged import set_copy_mode
 
     set_copy_mode(request.param)

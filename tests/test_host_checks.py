@@ -2,6 +2,8 @@
 with RuntimeError (there is no CPU path), bad boxes / dtypes / shapes raise before any launch, and the C ABI
 rejects bad sizes with QE_ERR_INVALID (ValueError) without touching the GPU."""
 
+import ctypes
+
 import pytest
 import torch
 
@@ -59,7 +61,14 @@ def test_c_abi_rejects_bad_sizes_without_a_gpu():
     with pytest.raises(ValueError):
         _lib.call("qe_gather_slots_heads", planes, 1, planes, 1, 48, 32, 16, 16, None, 1, None, None)
     for fn, bad in (("qe_set_norm_table_mode", 3), ("qe_set_silu_table_mode", 3), ("qe_set_silu_pipeline", 3),
-                    ("qe_set_paged_copy_mode", 4)):
+                    ("qe_set_paged_copy_mode", 5)):
         with pytest.raises(ValueError):
             _lib.call(fn, bad)
 
+
+
+def test_no_alloc_append_rejects_a_null_source_pointer():
+    host = (ctypes.c_void_p * 2)(4096, None)
+    with pytest.raises(ValueError, match="null source pointer 1"):
+        _lib.call("qe_append_slots_ptrs_noalloc", _lib.planes(16, 0, 0, 1), 4, ctypes.cast(host, ctypes.c_void_p), 2,
+                  16, 16, 1, None, None)

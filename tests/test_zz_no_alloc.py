@@ -67,6 +67,33 @@ def test_no_alloc_append_matches_the_allocating_one_twice():
         assert torch.equal(pool_b, ref)
 
 
+def test_no_alloc_append_with_16_byte_aligned_sources():
+    """Source rows that start 16 bytes past a 32-byte boundary: the copy falls back to 16-byte vectors and the
+    pool still equals the per-layer index_copy_."""
+    g = torch.Generator(device=DEV).manual_seed(2)
+    pool = torch.randn(L, 2, ROWS, H, D, generator=g, device=DEV).bfloat16()
+    n = 250
+    slots = torch.from_numpy(np.random.default_rng(1).permutation(ROWS)[:n].astype(np.int64)).to(DEV)
+    srcs = []
+    for t in _sources(20, n):
+        buf = torch.empty(t.numel() + 8, dtype=torch.bfloat16, device=DEV)
+        view = buf[8:].view(t.shape)
+        view.copy_(t)
+        assert view.data_ptr() % 32 == 16
+        srcs.append(view)
+    ref = pool.clone()
+    for layer in range(L):
+        ref[layer, 0].index_copy_(0, slots, srcs[2 * layer])
+        ref[layer, 1].index_copy_(0, slots, srcs[2 * layer + 1])
+    host = (ctypes.c_void_p * (2 * L))(*[t.data_ptr() for t in srcs])
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _lib.call("qe_append_slots_ptrs_noalloc", _planes(pool), ROWS, ctypes.cast(host, ctypes.c_void_p), 2 * L,
+              H * D * 2, slots.data_ptr(), n, err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert torch.equal(pool, ref)
+
+
 def test_no_alloc_append_rejects_more_planes_than_its_table():
     pool = torch.zeros(1, 2, 4, 1, 8, dtype=torch.bfloat16, device=DEV)
     host = (ctypes.c_void_p * 1025)()
