@@ -7,8 +7,10 @@
 //
 // A pool is a stack of planes (layer x {K,V}), each [rows, row_bytes]; a token's K or V for one layer is
 // one row of H*D elements (6 KB for the Qwen-Image DiT, 1 KB for the text encoder). Every row copy is
-// a 16-byte-vectorised, fully coalesced warp copy: lane i moves bytes [16 i, 16 i + 16) of each 512-byte
-// stripe, with 8 or 16 loads in flight per lane before the matching stores. Each warp walks its
+// a vectorised, fully coalesced warp copy, all loads of a pass issued before the matching stores: rows above
+// 1 KiB on 32-byte aligned planes move in 256-bit vectors (lane i: bytes [32 i, 32 i + 32) of each 1 KiB
+// stripe, 8 in flight per lane), other rows in 16-byte vectors (lane i: bytes [16 i, 16 i + 16) of each
+// 512-byte stripe, 8 or 16 in flight per lane; rows of at most 1 KiB several per warp pass). Each warp walks its
 // rows through the slot list (token-granular, page_size 1) or the block table (page_size P). The grid is
 // persistent: a multiple of the SM count, warps striding over the (plane, token) rows.
 #include <algorithm>
