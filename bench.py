@@ -349,11 +349,11 @@ def extras(pool, sess, device):
 
     out = {}
     peak, _ = measured_peak()
-    # both paged-copy kernels on the 1K turn's gather and append
+    # the paged-copy kernels (warp copy with 256-bit or 16-byte vectors, TMA bulk) on the 1K turn's gather and append
     m = pool.match(sess.vids(sess.turn))
     slots = pool.alloc(APPEND)
     variants = {}
-    for mode in ("warp", "bulk"):
+    for mode in ("warp", "warp16", "bulk"):
         set_copy_mode(mode)
         g_ms = _time_kernel(lambda: pool.gather_into(m.indices, sess.out), None, iters=5)
         a_ms = _time_kernel(lambda: pool.write(slots, sess.new_kv), None, iters=5)
