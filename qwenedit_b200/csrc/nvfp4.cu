@@ -479,30 +479,39 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     __syncthreads();
     tmem_fence_after_sync();
     tlane = *tmem_slot + (uint32_t(32 * (wid & 3)) << 16);
-    {  // the kWarps / 4 warps of each lane quarter share the writes of that quarter's copy
+    {  // the kWarps / 4 warps of each lane quarter share the writes of that quarter's copy. Table row r of
+       // group i sits at column 8 kGpl r + 8 i: r = 0 is w, r = 1 + t the bf16(1 + scale) row t, r = 1 + mod_rows
+       // + t the shift row t. A writer loads every row of its group before storing any, so the global loads are
+       // in flight together instead of one by one behind the stores.
       constexpr int kWriters = kWarps / 4;
+      constexpr int kMaxRows = int(kTmemCols) / (8 * kGpl);  // rows that fit the allocation (checked by the host)
+      const int rows = 1 + mod_rows * (kShift ? 2 : 1);
 #pragma unroll
       for (int i = 0; i < kGpl; ++i) {
         if (i % kWriters != (wid >> 2) % kWriters) continue;
         const int g = lane + 32 * i;
-        uint32_t v[8];
-        unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), v);
-        tmem_st8(tlane + 8 * i, v);
-        for (int t = 0; t < mod_rows; ++t) {
+        uint32_t v[kMaxRows][8];
+        unpack16(__ldg(p.w + 2 * g), __ldg(p.w + 2 * g + 1), v[0]);
+#pragma unroll
+        for (int r = 1; r < kMaxRows; ++r) {
+          if (r >= rows) break;
+          const bool is_shift = r > mod_rows;
+          const int t = is_shift ? r - 1 - mod_rows : r - 1;
           const int bt = t / p.variants;
           const bool noisy = (t % p.variants) == 0;
-          const __nv_bfloat16 *mrow = (noisy ? p.noisy : p.clean) + bt * p.mod_stride;
-          load_mod8(mrow, int64_t(g) * 16, p.mods_vec, v);
-          load_mod8(mrow, int64_t(g) * 16 + 8, p.mods_vec, v + 4);
+          const __nv_bfloat16 *row =
+              (is_shift ? (noisy ? p.shift : p.shift_clean) : (noisy ? p.noisy : p.clean)) + bt * p.mod_stride;
+          load_mod8(row, int64_t(g) * 16, p.mods_vec, v[r]);
+          load_mod8(row, int64_t(g) * 16 + 8, p.mods_vec, v[r] + 4);
+        }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) v[k] = badd2(kOne2, v[k]);
-          tmem_st8(tlane + 8 * kGpl * (1 + t) + 8 * i, v);
-          if (kShift) {
-            const __nv_bfloat16 *srow = (noisy ? p.shift : p.shift_clean) + bt * p.mod_stride;
-            load_mod8(srow, int64_t(g) * 16, p.mods_vec, v);
-            load_mod8(srow, int64_t(g) * 16 + 8, p.mods_vec, v + 4);
-            tmem_st8(tlane + 8 * kGpl * (1 + mod_rows + t) + 8 * i, v);
+        for (int r = 0; r < kMaxRows; ++r) {
+          if (r >= rows) break;
+          if (r >= 1 && r <= mod_rows) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[r][k] = badd2(kOne2, v[r][k]);
           }
+          tmem_st8(tlane + 8 * kGpl * r + 8 * i, v[r]);
         }
       }
       tmem_wait_st();

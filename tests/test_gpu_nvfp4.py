@@ -5,6 +5,7 @@ shapes, the reference test's shapes (tests/test_fibo_fp4.py:39-58) and edge case
 Tolerance (stated by the build's spec for NVFP4): bit-exact codes and scales, or <= 1 code step on <= 1e-4 of
 elements with the dequantised max-abs error reported. These tests require bit-exact."""
 
+import functools
 import json
 from pathlib import Path
 from types import SimpleNamespace
@@ -103,9 +104,39 @@ def test_norm_scale_widths_masks_batches(K):
 @pytest.mark.parametrize("B,masked,shift", [(1, True, True), (2, True, False), (2, False, True), (4, False, False),
                                             (3, False, True), (5, False, False)])
 def test_norm_scale_k3072_table_layouts(B, masked, shift, table_mode):
-    """K = 3072 with 1-5 modulation rows (x2 with a mask, x2 with a shift): the specialised kernel with its
-    constants in tensor memory (up to 256 columns) or in shared memory, bit-exact either way."""
+    """K = 3072 with 1-5 modulation rows (x2 with a mask, x2 with a shift) at 300 rows per batch: the specialised
+    kernel with its constants in shared or global memory (tensor memory takes them from 12,288 rows, which
+    test_norm_scale_k3072_tmem_layouts covers), bit-exact in each."""
     out, q_ref, sf_ref = _norm_case(B, 300, 3072, 1e-6, masked, shift, seed=B * 10 + masked * 2 + shift)
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@functools.lru_cache(maxsize=None)
+def _large_norm_case(B, masked, shift):
+    """Inputs and oracle outputs for K = 3072 with B x S >= 12,288 rows (the size from which the constants go to
+    tensor memory); x comes from a seeded torch generator (fast at this size), the rest from the fixtures."""
+    K, S, seed = 3072, -(-12288 // B), 100 + B * 10 + masked * 2 + shift
+    x = torch.randn(B, S, K, generator=torch.Generator().manual_seed(seed)).bfloat16()
+    w = inputs.bf16(seed + 1, (K,), scale=0.02, shift=1.0)
+    scale = inputs.bf16(seed + 2, (B, K), scale=0.1)
+    clean = inputs.bf16(seed + 3, (B, K), scale=0.1) if masked else None
+    mask = torch.from_numpy(inputs.uniforms(seed + 4, S) < 0.5) if masked else None
+    sh = inputs.bf16(seed + 5, (B, K), scale=0.1) if shift else None
+    sh_clean = inputs.bf16(seed + 6, (B, K), scale=0.1) if (shift and masked) else None
+    gs = nvfp4_ref.global_scale(nvfp4_ref.bf16_values_norm_scale(x, w, 1e-6, scale, clean, mask, sh, sh_clean))
+    q_ref, sf_ref = nvfp4_ref.norm_scale_fp4_ref(x, w, 1e-6, scale, clean, mask, gs, sh, sh_clean)
+    return (x, w, scale, clean, mask, sh, sh_clean, gs), q_ref, sf_ref
+
+
+@pytest.mark.parametrize("B,masked,shift", [(1, True, True), (2, True, False), (2, False, True), (4, False, False)])
+def test_norm_scale_k3072_tmem_layouts(B, masked, shift, table_mode):
+    """K = 3072 at 12,288+ rows with 2-5 constant rows per group (w, then bf16(1 + scale) and shift rows per batch
+    and mask variant): the layouts that fill the 256 tensor-memory columns, in every home, bit-exact."""
+    (x, w, scale, clean, mask, sh, sh_clean, gs), q_ref, sf_ref = _large_norm_case(B, masked, shift)
+    to = lambda t: None if t is None else t.to(DEV)  # noqa: E731
+    out = norm_scale_fp4(to(x), SimpleNamespace(weight=to(w), eps=1e-6), to(scale), to(clean), to(mask), _gs(gs),
+                         shift=to(sh), shift_clean=to(sh_clean))
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 
