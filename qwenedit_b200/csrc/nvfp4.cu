@@ -749,9 +749,11 @@ int launch_norm_k(int tab, bool shift, int warps, const NormParams &p, size_t sm
 // 2: always global memory
 std::atomic<int> g_norm_table_mode{0};
 bool tmem_tables_enabled() { return g_norm_table_mode.load(std::memory_order_relaxed) == 0; }
-// Below this many rows the per-CTA TMEM setup (allocation, table writes, fences) costs more than the shared-
-// memory traffic it saves (K = 3072, device time: 20.3 vs 19.8 us at 8,192 rows, 31.1 vs 32.2 us at 16,384,
-// 52.3 vs 57.7 us at 32,768).
+// Below this many rows the per-CTA TMEM setup (allocation, table writes, fences) can cost more than the shared-
+// memory traffic it saves. K = 3072, device time TMEM vs shared memory, back to back: with 3 constant rows per
+// group (w, bf16(1 + scale), shift) equal at 4,096-6,144 rows, 18.1 vs 18.7 us at 8,192, 21.5 vs 22.2 us at
+// 10,240; with 5 (a token mask doubles the modulation rows) 21.0 vs 20.4 us at 8,192. From 12,288 rows TMEM wins
+// for every layout (52.1 vs 57.0 us at 32,768).
 constexpr int64_t kTmemMinRows = 12288;
 
 // SiLU table home: 0 = by size (default), 1 = shared memory, 2 = global memory through L1
