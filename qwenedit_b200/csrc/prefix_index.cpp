@@ -532,6 +532,15 @@ int qe_index_insert(qe_index *ix, const int64_t *key, const int64_t *slots, int6
   QE_CHECK_ARG(ix && out_present, "qe_index_insert: null argument");
   QE_CHECK_ARG(n >= 0, "qe_index_insert: negative length");
   QE_CHECK_ARG(n == 0 || (key && slots), "qe_index_insert: null key or slots");
+  {  // the stored slots are freed by eviction later without a check: reject out-of-range ones here, before
+     // the tree changes (page 0, slots 0 .. page_size - 1, is padding)
+    const qe::Index &x = ix->ix;
+    const int64_t stored = x.aligned(n), lo = x.page, hi = (x.num_pages + 1) * x.page;
+    for (int64_t i = 0; i < stored; ++i)
+      if (slots[i] < lo || slots[i] >= hi)
+        return fail(QE_ERR_INVALID, "qe_index_insert: slot %lld at position %lld outside [%lld, %lld)",
+                    (long long)slots[i], (long long)i, (long long)lo, (long long)hi);
+  }
   try {
     *out_present = ix->ix.insert(key, slots, n);
   } catch (const std::bad_alloc &) {

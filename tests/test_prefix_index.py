@@ -164,6 +164,11 @@ def test_misuse_raises():
         ours.index.unlock(12345)
     with pytest.raises(Exception, match="out of range or already free"):
         ours.index.free(np.array([999999], np.int64))
+    before = ours.usage()
+    for bad in (0, -3, 33, 999999):  # slot 0 is padding; this pool's slots are 1 .. 32
+        with pytest.raises(ValueError, match="outside"):
+            ours.index.insert(np.arange(100, 104), np.array([5, 6, bad, 7], np.int64))
+    assert ours.usage() == before and ours.match(np.arange(100, 104)).length == 0
 
 
 def test_clear_resets_everything():
