@@ -697,13 +697,13 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
 template <int kK, int kWarps, int kTab, bool kShift, bool kAmax>
 int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   auto kernel = norm_scale_fp4_kernel<kK, kWarps, kTab, kShift, kAmax>;
-  static bool attr_set[64] = {};
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_relaxed)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_status(e, "qe_norm_scale_fp4: smem attribute");
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_relaxed);
   }
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kWarps * 32, smem) != cudaSuccess || occ < 1)
@@ -1137,7 +1137,7 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
   const int sched = g_silu_pipeline.load(std::memory_order_relaxed);
   const size_t smem = (l1 ? 0 : size_t(kSiluTable) * 2) + kScaleTab * sizeof(float);
-  static bool attr_set[12][64] = {};
+  static std::atomic<bool> attr_set[12][64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   using Kernel = void (*)(SiluParams);
@@ -1151,10 +1151,10 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   const int variant = sched * 4 + (amax ? 2 : 0) + (l1 ? 1 : 0);
   const Kernel kernel = kernels[variant];
   const int threads = silu_threads(sched);
-  if (!attr_set[variant][dev]) {
+  if (!attr_set[variant][dev].load(std::memory_order_relaxed)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_status(e, "qe_silu_mul_fp4: smem attribute");
-    attr_set[variant][dev] = true;
+    attr_set[variant][dev].store(true, std::memory_order_relaxed);
   }
   const int64_t items = M * ((K / 16 + 31) / 32);  // warp items: 32 groups of one row
   const int64_t warps_per_block = threads / 32;

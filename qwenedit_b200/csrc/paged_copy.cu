@@ -14,6 +14,7 @@
 // rows through the slot list (token-granular, page_size 1) or the block table (page_size P). The grid is
 // persistent: a multiple of the SM count, warps striding over the (plane, token) rows.
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "qe_cuda.cuh"
@@ -21,16 +22,16 @@
 namespace qe {
 
 int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];  // per device, filled on first use (relaxed: any thread may fill it)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cached[dev] = n;
+  int c = cached[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+    cached[dev].store(c, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return c;
 }
 
 namespace {
@@ -513,18 +514,18 @@ int bulk_launch_check(const CopyParams &p, int align) {
 
 // 0 auto, 1 warp LDG/STG, 2 TMA bulk, 3 warp LDG/STG with one row per warp pass, 4 warp LDG/STG with 16-byte
 // vectors only
-int g_copy_mode = 0;
+std::atomic<int> g_copy_mode{0};
 
 template <int kMode, bool kGather, bool kPtrs>
 int launch_bulk(const CopyParams &p, cudaStream_t stream) {
-  static bool attr_done[64] = {};
+  static std::atomic<bool> attr_done[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!attr_done[dev]) {
+  if (!attr_done[dev].load(std::memory_order_relaxed)) {
     cudaError_t e = cudaFuncSetAttribute(paged_bulk_kernel<kMode, kGather, kPtrs>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kStages * kChunk);
     if (e != cudaSuccess) return cuda_status(e, "paged bulk copy: smem attribute");
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_relaxed);
   }
   BulkGeom g{};
   if (kMode == kPages) {
@@ -543,14 +544,14 @@ int launch_bulk(const CopyParams &p, cudaStream_t stream) {
 
 template <typename V, int kMode, bool kGather, bool kPtrs, int kUnroll>
 int launch_unrolled(const CopyParams &p, cudaStream_t stream) {
-  static int blocks_per_sm = 0;
+  static std::atomic<int> cached_blocks{0};
+  int blocks_per_sm = cached_blocks.load(std::memory_order_relaxed);
   if (blocks_per_sm == 0) {
-    int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, paged_copy_kernel<V, kMode, kGather, kPtrs, kUnroll>,
-                                                      kThreads, 0) != cudaSuccess ||
-        b <= 0)
-      b = 2;
-    blocks_per_sm = b;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &blocks_per_sm, paged_copy_kernel<V, kMode, kGather, kPtrs, kUnroll>, kThreads, 0) != cudaSuccess ||
+        blocks_per_sm <= 0)
+      blocks_per_sm = 2;
+    cached_blocks.store(blocks_per_sm, std::memory_order_relaxed);
   }
   const int64_t rows = int64_t(p.n_planes) * p.n_tokens;
   const int64_t warps_per_block = kThreads / 32;
@@ -562,14 +563,14 @@ int launch_unrolled(const CopyParams &p, cudaStream_t stream) {
 
 template <typename V, int kMode, bool kGather, bool kPtrs>
 int launch_rows(const CopyParams &p, int rows_per_pass, cudaStream_t stream) {
-  static int blocks_per_sm = 0;
+  static std::atomic<int> cached_blocks{0};
+  int blocks_per_sm = cached_blocks.load(std::memory_order_relaxed);
   if (blocks_per_sm == 0) {
-    int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, paged_copy_rows_kernel<V, kMode, kGather, kPtrs>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, paged_copy_rows_kernel<V, kMode, kGather, kPtrs>,
                                                       kThreads, 0) != cudaSuccess ||
-        b <= 0)
-      b = 2;
-    blocks_per_sm = b;
+        blocks_per_sm <= 0)
+      blocks_per_sm = 2;
+    cached_blocks.store(blocks_per_sm, std::memory_order_relaxed);
   }
   const int64_t items = int64_t(p.n_planes) * ((p.n_tokens + rows_per_pass - 1) / rows_per_pass);
   const int64_t warps_per_block = kThreads / 32;
@@ -587,7 +588,8 @@ int launch_typed(const CopyParams &p, cudaStream_t stream) {
   // 768 B rows 0.86 of HBM vs 0.63 one row per pass; 1.5 KiB rows 0.87 vs 0.94 (the per-vector shuffle and row
   // arithmetic cost more than the extra loads in flight gain). g_copy_mode 3 forces the one-row kernel.
   const int64_t per_pass = std::min<int64_t>(32 * kRowsUnroll / std::max<int64_t>(vpr, 1), 32);
-  if (g_copy_mode != 3 && per_pass >= 8) return launch_rows<V, kMode, kGather, kPtrs>(p, int(per_pass), stream);
+  if (g_copy_mode.load(std::memory_order_relaxed) != 3 && per_pass >= 8)
+    return launch_rows<V, kMode, kGather, kPtrs>(p, int(per_pass), stream);
   if (vpr >= 32 * 12) return launch_unrolled<V, kMode, kGather, kPtrs, 16>(p, stream);
   return launch_unrolled<V, kMode, kGather, kPtrs, 8>(p, stream);
 }
@@ -598,10 +600,11 @@ bool planes_aligned(const qe_planes &pl, int a) {
 
 template <int kMode, bool kGather, bool kPtrs>
 int launch(const CopyParams &p, int align, cudaStream_t stream) {
-  if (g_copy_mode == 2 && bulk_launch_check(p, align)) return launch_bulk<kMode, kGather, kPtrs>(p, stream);
+  const int mode = g_copy_mode.load(std::memory_order_relaxed);
+  if (mode == 2 && bulk_launch_check(p, align)) return launch_bulk<kMode, kGather, kPtrs>(p, stream);
   // rows above 1 KiB (one row per warp pass) on 32-byte aligned planes: 256-bit vectors, 8 per lane in flight
   // (the same bytes as 16 of 16 bytes, half the instructions and L1 requests)
-  if (align >= 32 && g_copy_mode != 4 && (p.row_bytes > 1024 || g_copy_mode == 3))
+  if (align >= 32 && mode != 4 && (p.row_bytes > 1024 || mode == 3))
     return launch_unrolled<Vec32, kMode, kGather, kPtrs, 8>(p, stream);
   if (align >= 16) return launch_typed<int4, kMode, kGather, kPtrs>(p, stream);
   if (align >= 4) return launch_typed<uint32_t, kMode, kGather, kPtrs>(p, stream);
@@ -784,7 +787,7 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
 
 int qe_set_paged_copy_mode(int32_t mode) {
   if (mode < 0 || mode > 4) return fail(QE_ERR_INVALID, "qe_set_paged_copy_mode: mode must be 0, 1, 2, 3 or 4");
-  qe::g_copy_mode = mode;
+  qe::g_copy_mode.store(mode, std::memory_order_relaxed);
   return qe::ok();
 }
 
@@ -806,18 +809,20 @@ static __device__ __align__(256) const void *g_static_src_ptrs[qe::kStaticMaxPla
 namespace qe {
 namespace {
 int static_ptr_table(const void *const **out) {
-  static const void *const *addr[64] = {};
+  static std::atomic<const void *const *> addr[64];  // per device: the table's device address
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "qe_append_slots_ptrs_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: device %d above 63", dev);
-  if (!addr[dev]) {
+  const void *const *table = addr[dev].load(std::memory_order_relaxed);
+  if (!table) {
     void *ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_static_src_ptrs);
     if (e != cudaSuccess) return cuda_status(e, "qe_append_slots_ptrs_noalloc: cudaGetSymbolAddress");
-    addr[dev] = static_cast<const void *const *>(ptr);
+    table = static_cast<const void *const *>(ptr);
+    addr[dev].store(table, std::memory_order_relaxed);
   }
-  *out = addr[dev];
+  *out = table;
   return QE_OK;
 }
 }  // namespace
