@@ -72,3 +72,68 @@ def test_no_alloc_append_rejects_a_null_source_pointer():
     with pytest.raises(ValueError, match="null source pointer 1"):
         _lib.call("qe_append_slots_ptrs_noalloc", _lib.planes(16, 0, 0, 1), 4, ctypes.cast(host, ctypes.c_void_p), 2,
                   16, 16, 1, None, None)
+
+
+A = 0x10000  # a 64 KiB-aligned stand-in address: every call below fails its checks before touching it
+
+
+def _rejects(name, match, *args):
+    with pytest.raises(ValueError, match=match):
+        _lib.call(name, *args)
+
+
+def test_nvfp4_entry_points_check_sizes_and_alignment_first():
+    """The NVFP4 entry points reject bad sizes, missing operands and misaligned pointers with QE_ERR_INVALID
+    before any CUDA call (each case below breaks exactly one rule)."""
+    base = dict(x=A, w=A, noisy=A, clean=None, mask=None, shift=None, shift_clean=None, gs=A, M=128, S=128,
+                K=3072, mod_stride=0, eps=1e-6, q=A, sf=A, stream=None)
+
+    def norm(match, **change):
+        a = dict(base, **change)
+        _rejects("qe_norm_scale_fp4", match, *a.values())
+
+    norm("null argument", w=None)
+    norm("needs `clean`", mask=A)
+    norm("needs `shift_clean`", mask=A, clean=A, shift=A)
+    norm("bad sizes", S=0)
+    norm("multiple of 64", K=100)
+    norm("above the supported", K=16448)
+    norm("x must be 16-byte aligned", x=A + 8)
+    norm("not a multiple of S", M=130)
+    norm("negative mod_stride", mod_stride=-1)
+    norm("x and w must be 16-byte aligned", w=A + 8)
+    norm("q must be 8-byte", q=A + 4)
+    norm("sf 4-byte", sf=A + 2)
+    _rejects("qe_norm_scale_amax", "null amax", A, A, A, None, None, None, None, 128, 128, 3072, 0, 1e-6, None, None)
+
+    silu = dict(gate=A, value=A, gs=A, M=128, K=12288, q=A, sf=A, table=A, stream=None)
+
+    def silu_call(match, **change):
+        a = dict(silu, **change)
+        _rejects("qe_silu_mul_fp4", match, *a.values())
+
+    silu_call("null argument", table=None)
+    silu_call("bad sizes", M=-1)
+    silu_call("multiple of 64", K=100)
+    silu_call("16-byte aligned", gate=A + 8)
+    silu_call("16-byte aligned", value=A + 8)
+    silu_call("q must be 8-byte", q=A + 4)
+    _rejects("qe_silu_mul_amax", "null amax", A, A, 128, 12288, A, None, None)
+    _rejects("qe_silu_table_init", "16-byte aligned", A + 8, None)
+
+
+def test_scatter_append_checks_its_geometry_first():
+    peers = (ctypes.c_void_p * 2)(A, A)
+    pl = _lib.planes(A, 0, 0, 1)
+    err = A
+
+    def scatter(match, n_peers=2, slice_bytes=16, pool=pl, src=pl, n_tokens=1):
+        _rejects("qe_append_scatter", match, ctypes.cast(peers, ctypes.c_void_p), n_peers, pool, 4, src, 1,
+                 slice_bytes, A, n_tokens, err, None)
+
+    scatter("1..8 peer pools", n_peers=9)
+    scatter("1..8 peer pools", n_peers=0)
+    scatter("multiple of 16", slice_bytes=8)
+    scatter("planes_inner", src=_lib.planes(A, 0, 0, 0))
+    scatter("multiples of 16 bytes", pool=_lib.planes(A, 24, 0, 1))
+    scatter("source must be 16-byte aligned", src=_lib.planes(A + 8, 0, 0, 1))
