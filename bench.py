@@ -399,7 +399,7 @@ def extras(pool, sess, device):
 
 
 def index_latency(turns: int = 40, page: int = PAGE) -> dict:
-    """Host latency of the prefix index per 1K-edit turn (SURVEY-style: reported as latency, not bandwidth):
+    """Host latency of the prefix index per 1K-edit turn (reported as latency, not bandwidth):
     match of the 4,608-token prefix, alloc of the 4,096 new tokens (with LRU eviction once the 24 GiB pool is
     full), insert of the next prefix, release. The native index (libqeb200) against the oracle's Python
     restatement of the reference's tree (SGLang RadixCache + allocator), both index-only (no device data)."""

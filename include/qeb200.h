@@ -54,6 +54,9 @@ const char *qe_version(void);
  * Requirements: row_bytes, strides and base pointers multiples of 16 bytes; slots / pages in range
  * (checked on the device: an out-of-range slot is skipped and reported through *err_flag when
  * err_flag is non-null; pass the pool's row count in pool_rows).
+ * *err_flag bits (OR-ed by the device, never cleared by it): 1 = a slot or page out of range (row skipped),
+ * 2 = a bounded wait of the bulk-copy kernel gave up, 4 = a per-plane source pointer (pointer forms) null or
+ * misaligned (plane skipped).
  */
 typedef struct qe_planes {
   void *base;            /* device pointer of plane 0 */
@@ -85,7 +88,9 @@ int qe_append_pages(qe_planes pool, int64_t pool_rows, qe_planes src, int32_t n_
 
 /* append from one source pointer per plane (hooks.py:136-138: 2*L separate index_copy_ calls from
  * the per-layer caches layer["key"][0] / layer["value"][0]) in ONE launch. src_ptrs is a DEVICE
- * array of n_planes device pointers; each source plane is row-contiguous ([n_tokens, row_bytes]). */
+ * array of n_planes device pointers; each source plane is row-contiguous ([n_tokens, row_bytes]).
+ * Every source pointer must be 16-byte aligned (the host cannot see them; the kernel checks each one against
+ * the vector width it was launched with and skips a null or misaligned plane, setting bit 4 of *err_flag). */
 int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs, int32_t n_planes,
                          int64_t row_bytes, const int64_t *slots, int64_t n_tokens, int32_t *err_flag,
                          void *stream);
@@ -99,10 +104,12 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
  * with QE_ERR_INVALID before any work. The first call on each device looks the table up with
  * cudaGetSymbolAddress, so make that first call before any stream capture. Every call rewrites the table's
  * first n_planes entries on `stream` and the kernel reads them from there: calls whose work can overlap on the
- * GPU (different streams) race on the shared table; issue them on one stream. Allocates nothing: no cudaMalloc,
- * cudaFree or allocating library call. The host array is copied with cudaMemcpyAsync: pageable memory may be
- * reused once the call returns, pinned memory once `stream` has passed the call. Null source pointers are
- * rejected; the vector width follows the least-aligned source pointer. */
+ * GPU (different streams) race on the shared table; issue them on one stream. Host threads calling on one stream
+ * are serialised by a per-device lock held from the table write through the launch, so their table writes and
+ * kernels cannot interleave. Allocates nothing: no cudaMalloc, cudaFree or allocating library call. The host
+ * array is copied with cudaMemcpyAsync: pageable memory may be reused once the call returns, pinned memory once
+ * `stream` has passed the call. Null source pointers are rejected; the vector width follows the least-aligned
+ * source pointer. */
 int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *const *src_ptrs_host,
                                  int32_t n_planes, int64_t row_bytes, const int64_t *slots, int64_t n_tokens,
                                  int32_t *err_flag, void *stream);

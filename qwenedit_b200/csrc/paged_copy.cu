@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "qe_cuda.cuh"
 
@@ -62,6 +63,21 @@ struct CopyParams {
 };
 
 enum { kSlots = 0, kPages = 1 };
+
+// Error-flag bits a copy kernel may set: an out-of-range slot or page (that row is skipped), a bounded wait that
+// gave up (bulk kernel), and a per-plane source pointer (pointer form) that is null or not aligned to the
+// vector width the launch chose (that plane is skipped: a misaligned vector load would fault the kernel).
+constexpr int32_t kErrSlot = 1, kErrTimeout = 2, kErrSrcPtr = 4;
+
+// Pointer form: the source plane's base, or null when it is null or not `align`-byte aligned (flagged).
+__device__ __forceinline__ const char *checked_src(const CopyParams &p, int32_t plane, uint32_t align, bool report) {
+  const char *ptr = static_cast<const char *>(p.other_ptrs[plane]);
+  if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & (align - 1u)) != 0) {
+    if (report && p.err) atomicOr(p.err, kErrSrcPtr);
+    return nullptr;
+  }
+  return ptr;
+}
 
 // 32 bytes: one 256-bit load / store per lane (sm_100), so a warp request covers 1 KiB
 struct alignas(32) Vec32 {
@@ -121,13 +137,15 @@ __global__ void __launch_bounds__(kThreads) paged_copy_kernel(CopyParams p) {
       slot = page * p.page_size + t % p.page_size;
     }
     if (slot < 0 || slot >= p.pool_rows) {  // out-of-range slot: skip the row, report it
-      if (lane == 0 && p.err) atomicOr(p.err, 1);
+      if (lane == 0 && p.err) atomicOr(p.err, kErrSlot);
       continue;
     }
     char *pool_row = p.pool.plane(plane) + slot * p.row_bytes;
     const char *other_row;
     if (kPtrs) {
-      other_row = static_cast<const char *>(p.other_ptrs[plane]) + t * p.row_bytes;
+      const char *src_plane = checked_src(p, plane, sizeof(V), lane == 0);
+      if (src_plane == nullptr) continue;  // null or misaligned source plane: skipped, reported
+      other_row = src_plane + t * p.row_bytes;
     } else {
       other_row = p.other.plane(plane) + t * p.row_bytes;
     }
@@ -179,13 +197,14 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
         my_slot = int64_t(__ldg(p.pages + t / p.page_size)) * p.page_size + t % p.page_size;
       }
       if (my_slot < 0 || my_slot >= p.pool_rows) {
-        if (p.err) atomicOr(p.err, 1);
+        if (p.err) atomicOr(p.err, kErrSlot);
         my_slot = -2;  // skipped
       }
     }
     char *pool_plane = p.pool.plane(plane);
     const char *other_plane =
-        kPtrs ? static_cast<const char *>(p.other_ptrs[plane]) : static_cast<const char *>(p.other.plane(plane));
+        kPtrs ? checked_src(p, plane, sizeof(V), lane == 0) : static_cast<const char *>(p.other.plane(plane));
+    if (other_plane == nullptr) continue;  // pointer form: null or misaligned source plane, skipped and reported
     // the R rows of the pass are one run on the contiguous side: vector v of the pass is run[v]
     V *run = reinterpret_cast<V *>(const_cast<char *>(other_plane) + t0 * p.row_bytes);
     V buf[kRowsUnroll];
@@ -258,7 +277,7 @@ __global__ void __launch_bounds__(kThreads) gather_heads_kernel(HeadsParams p) {
     if (lane < R && t0 + lane < p.n_tokens) {
       my_slot = __ldg(p.slots + t0 + lane);
       if (my_slot < 0 || my_slot >= p.pool_rows) {
-        if (p.err) atomicOr(p.err, 1);
+        if (p.err) atomicOr(p.err, kErrSlot);
         my_slot = -2;
       }
     }
@@ -372,7 +391,8 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
   const int32_t plane = int32_t(c / g.chunks_per_plane);
   const int64_t rem = c - int64_t(plane) * g.chunks_per_plane;
   char *pool_plane = p.pool.plane(plane);
-  char *oth_plane = kPtrs ? static_cast<char *>(const_cast<void *>(p.other_ptrs[plane])) : p.other.plane(plane);
+  char *oth_plane = kPtrs ? const_cast<char *>(checked_src(p, plane, 16, false)) : p.other.plane(plane);
+  if (kPtrs && oth_plane == nullptr) return 0;  // skipped plane (reported by bulk_chunk_bytes)
   if (kMode == kPages) {
     const int64_t run = rem / g.chunks_per_run;
     const int64_t k = rem - run * g.chunks_per_run;
@@ -384,7 +404,7 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
     const uint32_t bytes = uint32_t(min(int64_t(kChunk), run_bytes - off));
     const int64_t page = __ldg(p.pages + run);
     if (page < 0 || (page + 1) * p.page_size > p.pool_rows) {
-      if (kLoad && p.err) atomicOr(p.err, 1);
+      if (kLoad && p.err) atomicOr(p.err, kErrSlot);
       return 0;
     }
     char *pool_ptr = pool_plane + page * p.page_size * p.row_bytes + off;
@@ -414,7 +434,7 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
     for (int64_t i = 0; i < rows; ++i) {
       const int64_t slot = __ldg(p.slots + t0 + i);
       if (slot < 0 || slot >= p.pool_rows) {
-        if (kLoad && p.err) atomicOr(p.err, 1);
+        if (kLoad && p.err) atomicOr(p.err, kErrSlot);
         continue;  // skipped row: its bytes are not expected
       }
       char *pool_ptr = pool_plane + slot * p.row_bytes;
@@ -431,10 +451,11 @@ __device__ __forceinline__ uint32_t bulk_chunk(const CopyParams &p, const BulkGe
 }
 
 // bytes the loads of chunk c will deliver (the mbarrier's transaction count), computed before issuing
-template <int kMode, bool kGather>
+template <int kMode, bool kGather, bool kPtrs>
 __device__ __forceinline__ uint32_t bulk_chunk_bytes(const CopyParams &p, const BulkGeom &g, int64_t c) {
   const int32_t plane = int32_t(c / g.chunks_per_plane);
   const int64_t rem = c - int64_t(plane) * g.chunks_per_plane;
+  if (kPtrs && checked_src(p, plane, 16, true) == nullptr) return 0;  // null or misaligned source plane
   if (kMode == kPages) {
     const int64_t run = rem / g.chunks_per_run;
     const int64_t k = rem - run * g.chunks_per_run;
@@ -475,7 +496,7 @@ __global__ void __launch_bounds__(32) paged_bulk_kernel(CopyParams p, BulkGeom g
     const int64_t c = first + i * stride;
     const uint32_t s = uint32_t(i % kStages);
     const uint32_t bar = smem_u32(&bars[s]);
-    const uint32_t bytes = bulk_chunk_bytes<kMode, kGather>(p, g, c);
+    const uint32_t bytes = bulk_chunk_bytes<kMode, kGather, kPtrs>(p, g, c);
     mbar_expect(bar, bytes);
     if (bytes) bulk_chunk<kMode, kGather, kPtrs, true>(p, g, c, base + s * kChunk, bar);
   };
@@ -499,7 +520,7 @@ __global__ void __launch_bounds__(32) paged_bulk_kernel(CopyParams p, BulkGeom g
     }
   }
   if (!ok) {
-    if (p.err) atomicOr(p.err, 2);
+    if (p.err) atomicOr(p.err, kErrTimeout);
     // drain the loads still in flight (each wait bounded again) so no copy lands in a retired CTA
     const int64_t issued = min(mine, (i >= 1 ? i - 1 + kStages : int64_t(kStages)));
     for (int64_t j = i; j < issued; ++j) mbar_wait(smem_u32(&bars[j % kStages]), uint32_t((j / kStages) & 1));
@@ -808,12 +829,17 @@ static __device__ __align__(256) const void *g_static_src_ptrs[qe::kStaticMaxPla
 
 namespace qe {
 namespace {
-int static_ptr_table(const void *const **out) {
+// One lock per device, held from the table write through the kernel launch, so that two host threads issuing on
+// the same stream cannot interleave as write A, write B, kernel A, kernel B (kernel A would read B's pointers).
+std::mutex g_static_table_lock[64];
+
+int static_ptr_table(int *dev_out, const void *const **out) {
   static std::atomic<const void *const *> addr[64];  // per device: the table's device address
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "qe_append_slots_ptrs_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(QE_ERR_INVALID, "qe_append_slots_ptrs_noalloc: device %d above 63", dev);
+  *dev_out = dev;
   const void *const *table = addr[dev].load(std::memory_order_relaxed);
   if (!table) {
     void *ptr = nullptr;
@@ -846,11 +872,14 @@ extern "C" int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, c
       align = align == 32 ? 16 : align == 16 ? 4 : 1;
   }
   const void *const *table = nullptr;
-  s = qe::static_ptr_table(&table);
+  int dev = 0;
+  s = qe::static_ptr_table(&dev, &table);
   if (s) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the table is written on the caller's stream ahead of the kernel that reads it; the host array may be
-  // reused as soon as this call returns
+  std::lock_guard<std::mutex> hold(qe::g_static_table_lock[dev]);
+  // The table is written on the caller's stream ahead of the kernel that reads it. A pageable host array is
+  // staged by the copy before this call returns; a pinned one is read by the GPU when the stream reaches the
+  // copy, so it must stay unchanged until then.
   s = qe::cuda_status(cudaMemcpyAsync(const_cast<const void **>(table), src_ptrs_host, size_t(n_planes) * sizeof(void *),
                                       cudaMemcpyHostToDevice, st),
                       "qe_append_slots_ptrs_noalloc: pointer table copy");

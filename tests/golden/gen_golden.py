@@ -1,6 +1,6 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE (QwenEdit) code itself.
 
-    python -m tests.golden.gen_golden [--reference /root/reference]
+    python -m tests.golden.gen_golden --reference <QwenEdit checkout>   (or QWENEDIT_REFERENCE=<checkout>)
 
 Runs only where the reference checkout exists (it is read, never modified); the fixtures it writes are what
 the tests use everywhere else. What it runs:
@@ -303,7 +303,9 @@ def hash_seed(name: str) -> int:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("QWENEDIT_REFERENCE"),
+                    required="QWENEDIT_REFERENCE" not in os.environ,
+                    help="path of a QwenEdit checkout (default: $QWENEDIT_REFERENCE)")
     ap.add_argument("--only", choices=["keys", "nvfp4", "paged", "latents"], default=None)
     args = ap.parse_args()
     import_reference(Path(args.reference))

@@ -207,6 +207,39 @@ def test_write_layers_matches_per_layer_index_copy():
     assert torch.equal(pool.kv.cpu(), ref)
 
 
+def test_pointer_append_skips_and_flags_a_misaligned_source():
+    """qe_append_slots_ptrs through the C ABI with one source plane starting 2 bytes past a 16-byte boundary:
+    the kernel sets bit 4 of the error flag and leaves that plane's pool rows untouched instead of issuing
+    misaligned vector loads; every other plane equals the per-layer index_copy_."""
+    from qwenedit_b200 import _lib
+
+    L, H, D = 3, 24, 128
+    pool = _pool(L, H, D, 600, torch.bfloat16, seed=31)
+    n = 111
+    idx = _slots(32, n, pool.rows)
+    srcs = [inputs.f32(300 + i, (n, H, D)).bfloat16().to(DEV) for i in range(2 * L)]
+    bad = 3  # layer 1, V
+    buf = torch.empty(n * H * D + 1, dtype=torch.bfloat16, device=DEV)
+    shifted = buf[1:].view(n, H, D)
+    shifted.copy_(srcs[bad])
+    assert shifted.data_ptr() % 16 == 2
+    ptrs = [t.data_ptr() for t in srcs]
+    ptrs[bad] = shifted.data_ptr()
+    table = torch.tensor(ptrs, dtype=torch.int64, device=DEV)
+    ref = pool.kv.cpu().clone()
+    for p in range(2 * L):
+        if p != bad:
+            ref[p // 2, p % 2].index_copy_(0, idx, srcs[p].cpu())
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv = pool.kv
+    planes = _lib.planes(kv.data_ptr(), kv.stride(0) * 2, kv.stride(1) * 2, 2)
+    _lib.call("qe_append_slots_ptrs", planes, pool.rows, table.data_ptr(), 2 * L, H * D * 2,
+              idx.to(DEV).data_ptr(), n, err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert err.item() & 4
+    assert torch.equal(pool.kv.cpu(), ref)
+
+
 def test_encoder_extra_rows():
     """encoder.py:114 (extra.index_select) and :135 (extra.index_copy_); encoder geometry 28 x 4 x 128 + 3584."""
     pool = _pool(28, 4, 128, 300, torch.bfloat16, extra=3584, seed=9)

@@ -40,3 +40,48 @@ def test_environment_defaults():
     assert state.MIN_REUSE == 256 and state.ENC_MIN_REUSE == 128
     assert state.KV_PAGE >= 1 and state.ENC_PAGE >= 1
     assert state.OUTPUT_LATENTS.capacity == 512
+
+
+def test_settings_read_the_reference_variables():
+    env = {"MULTI_TURN_PREFIX_CACHE": "0", "MULTI_TURN_DEBUG": "1", "MULTI_TURN_MIN_REUSE": "64",
+           "MULTI_TURN_ENC_MIN_REUSE": "32", "MULTI_TURN_LATENT_SLOTS": "7", "MULTI_TURN_KV_GPU_GIB": "1.5",
+           "MULTI_TURN_ENC_GPU_GIB": "0.25", "MULTI_TURN_KV_PAGE": "64"}
+    s = state.Settings.from_env(env)
+    assert (s.prefix_cache, s.encoder_cache, s.debug) == (False, True, True)
+    assert (s.min_reuse, s.enc_min_reuse, s.latent_slots) == (64, 32, 7)
+    assert (s.dit_pool_gib, s.encoder_pool_gib, s.dit_page, s.encoder_page) == (1.5, 0.25, 64, 1)
+    assert state.Settings.from_env({}) == state.Settings()
+
+
+def test_pool_registry_builds_once_and_resets():
+    class FakePool:
+        def __init__(self):
+            self.cleared = 0
+
+        def usage(self):
+            return {"cleared": self.cleared}
+
+        def clear(self):
+            self.cleared += 1
+
+    reg = state.PoolRegistry()
+    built = []
+    first = reg.get_or_build("dit", lambda: built.append(1) or FakePool())
+    again = reg.get_or_build("dit", lambda: built.append(1) or FakePool())
+    assert first is again and built == [1]
+    assert reg.usage("encoder") is None and reg.usage("dit") == {"cleared": 0}
+    reg.clear_all()
+    assert reg.usage("dit") == {"cleared": 1}
+
+
+def test_key_roots_are_the_reference_tuples():
+    from types import SimpleNamespace
+
+    from qwenedit_b200 import keys
+
+    args = SimpleNamespace(model_path="/m", component_quantizations={"t": "fp4"}, transformer_quantization="fp4")
+    assert state.dit_root(args) == keys.root_key("dit", "/m", {"t": "fp4"}, "fp4", None)
+    enc = SimpleNamespace(text_encoder=SimpleNamespace(config=SimpleNamespace(_name_or_path="qwen-vl")))
+    assert state.encoder_root(enc) == keys.root_key("encoder", "qwen-vl", None)
+    u = state.usage()
+    assert set(u) == {"dit", "encoder", "output_latents", "vae_latents"}

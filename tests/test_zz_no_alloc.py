@@ -49,7 +49,17 @@ def _call_both(pool_a, pool_b, srcs, slots):
     return table
 
 
-def test_no_alloc_append_matches_the_allocating_one_twice():
+@pytest.fixture
+def copy_mode(request):
+    """Run under one of the copy kernels (0 default, 1 warp, 2 TMA bulk, 3 one row per pass, 4 16-byte
+    vectors); the default is restored afterwards."""
+    _lib.call("qe_set_paged_copy_mode", request.param)
+    yield request.param
+    _lib.call("qe_set_paged_copy_mode", 0)
+
+
+@pytest.mark.parametrize("copy_mode", [0, 1, 2, 3, 4], indirect=True)
+def test_no_alloc_append_matches_the_allocating_one_twice(copy_mode):
     g = torch.Generator(device=DEV).manual_seed(1)
     pool_a = torch.randn(L, 2, ROWS, H, D, generator=g, device=DEV).bfloat16()
     pool_b = pool_a.clone()
@@ -58,7 +68,7 @@ def test_no_alloc_append_matches_the_allocating_one_twice():
         slots = torch.from_numpy(rng.permutation(ROWS)[:n].astype(np.int64)).to(DEV)
         srcs = _sources(10 + call, n)
         _call_both(pool_a, pool_b, srcs, slots)
-        assert torch.equal(pool_a, pool_b), f"call {call}"
+        assert torch.equal(pool_a, pool_b), f"call {call}, copy mode {copy_mode}"
         # and both equal the per-layer index_copy_ the reference runs (hooks.py:136-138)
         ref = pool_a.clone()
         for layer in range(L):
