@@ -579,15 +579,25 @@ def _copies(nbytes_each: int) -> int:
 
 
 def nvfp4_extras(device, peak):
-    """NVFP4 producers at the benchmark shapes. `ms`: back-to-back launches from a CUDA graph, each on its own
-    input copy (HBM-resident); `ms_single_launch`: one launch between CUDA events after an L2 flush (includes
-    the launch latency)."""
+    """NVFP4 producers at the benchmark shapes (norm T = 4096 / 16384 / 32768 at K = 3072, SiLU T = 4096 / 16384 /
+    32768 at K = 12288). `ms`: back-to-back launches from a CUDA graph, each on its own input copy (HBM-resident);
+    `ms_single_launch`: one launch between CUDA events after an L2 flush (includes the launch latency).
+    `nvfp4_vs_triton`: the reference's own Triton kernels (fibo/fp4.py:64-116, from the offline install under
+    baseline/_ref) timed the same way on the same inputs, next to ours on identical work (no adaLN shift, which
+    the reference kernel does not have), with the encodings compared."""
     from types import SimpleNamespace
 
-    from qwenedit_b200.fp4 import norm_scale_amax, norm_scale_fp4, silu_mul_amax, silu_mul_fp4
+    from qwenedit_b200.fp4 import global_scale, norm_scale_amax, norm_scale_fp4, silu_mul_amax, silu_mul_fp4
 
+    try:
+        from baseline import reference_fp4
+
+        ref = reference_fp4.load()
+    except Exception as exc:  # noqa: BLE001
+        ref, reference_fp4 = None, None
+        ref_missing = f"{type(exc).__name__}: {exc}"
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2, rewritten between launches
-    out = {}
+    out, vs = {}, {}
 
     def record(name, nbytes, calls, single):
         ms = _time_graph(calls)
@@ -595,13 +605,21 @@ def nvfp4_extras(device, peak):
         out[name] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
                      "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4), "ms_single_launch": round(ms1, 4)}
 
+    def versus(name, nbytes, ours_calls, ref_calls, compare):
+        if ref is None:
+            return
+        ours_ms, ref_ms = _time_graph(ours_calls), _time_graph(ref_calls)
+        vs[name] = {"ours_ms": round(ours_ms, 4), "triton_ms": round(ref_ms, 4),
+                    "ours_GB/s": round(nbytes / ours_ms / 1e6, 1), "triton_GB/s": round(nbytes / ref_ms / 1e6, 1),
+                    "speedup": round(ref_ms / ours_ms, 3), "parity": compare()}
+
     K = 3072
     norm = SimpleNamespace(weight=(1 + 0.02 * torch.randn(K, device=device)).bfloat16(), eps=1e-6)
     scale = (0.1 * torch.randn(1, K, device=device)).bfloat16()
     shift = (0.1 * torch.randn(1, K, device=device)).bfloat16()
-    gs = torch.tensor([50.0], device=device)
-    for T in (4096, 32768):
+    for T in (4096, 16384, 32768):
         xs = [torch.randn(1, T, K, dtype=torch.bfloat16, device=device) for _ in range(_copies(T * K * 2))]
+        gs = global_scale(norm_scale_amax(xs[0], norm, scale, None, None, shift=shift))
         pad = -(-T // 128) * 128
         nbytes = T * K * 2 + K * 2 * 3 + T * K // 2 + pad * K // 16
         record(f"norm_scale_fp4_T{T}", nbytes,
@@ -611,12 +629,24 @@ def nvfp4_extras(device, peak):
             record(f"norm_scale_amax_T{T}", T * K * 2 + K * 2 * 3,
                    [lambda x=x: norm_scale_amax(x, norm, scale, None, None, shift=shift) for x in xs],
                    lambda: norm_scale_amax(xs[0], norm, scale, None, None, shift=shift))
+
+        def cmp_norm():
+            a = norm_scale_fp4(xs[0], norm, scale, None, None, gs)
+            b = ref.norm_scale_fp4(xs[0], norm, scale, None, None, gs)
+            st = reference_fp4.compare_nvfp4(a.q, a.sf, b.q, b.sf, gs.item(), T, K)
+            return {k: st[k] for k in ("bit_exact", "frac_elements_differing", "max_code_step_same_scale",
+                                       "dequant_max_abs_err")}
+
+        versus(f"norm_scale_fp4_T{T}", T * K * 2 + K * 2 * 2 + T * K // 2 + pad * K // 16,
+               [lambda x=x: norm_scale_fp4(x, norm, scale, None, None, gs) for x in xs],
+               [lambda x=x: ref.norm_scale_fp4(x, norm, scale, None, None, gs) for x in xs], cmp_norm)
         del xs
     K = 12288
-    for T in (4096, 16384):
+    for T in (4096, 16384, 32768):
         n = _copies(2 * T * K * 2)
         gv = [(torch.randn(T, K, dtype=torch.bfloat16, device=device),
                torch.randn(T, K, dtype=torch.bfloat16, device=device)) for _ in range(n)]
+        gs = global_scale(silu_mul_amax(gv[0][0], gv[0][1]))
         pad = -(-T // 128) * 128
         nbytes = 2 * T * K * 2 + T * K // 2 + pad * K // 16
         record(f"silu_mul_fp4_T{T}", nbytes, [lambda g=g, v=v: silu_mul_fp4(g, v, gs) for g, v in gv],
@@ -624,7 +654,18 @@ def nvfp4_extras(device, peak):
         if T == 16384:
             record(f"silu_mul_amax_T{T}", 2 * T * K * 2, [lambda g=g, v=v: silu_mul_amax(g, v) for g, v in gv],
                    lambda: silu_mul_amax(gv[0][0], gv[0][1]))
+
+        def cmp_silu():
+            a = silu_mul_fp4(gv[0][0], gv[0][1], gs)
+            b = ref.silu_mul_fp4(gv[0][0], gv[0][1], gs)
+            st = reference_fp4.compare_nvfp4(a.q, a.sf, b.q, b.sf, gs.item(), T, K)
+            return {k: st[k] for k in ("bit_exact", "frac_elements_differing", "max_code_step_same_scale",
+                                       "dequant_max_abs_err")}
+
+        versus(f"silu_mul_fp4_T{T}", nbytes, [lambda g=g, v=v: silu_mul_fp4(g, v, gs) for g, v in gv],
+               [lambda g=g, v=v: ref.silu_mul_fp4(g, v, gs) for g, v in gv], cmp_silu)
         del gv
+    out["nvfp4_vs_triton"] = vs if ref is not None else {"unavailable": ref_missing}
     return out
 
 
@@ -1019,13 +1060,14 @@ def main():
         if rank != 0:
             return
         gbs, per_turn, threads = cpu_turns(args.steps, args.warmup)
-        sample = (f"{CPU_SAMPLE_LAYERS} of {L} layers per turn (same per-layer shapes); "
-                  f"{args.steps} timed turns after {args.warmup} warm-up")
+        sample = (f"{CPU_SAMPLE_LAYERS} of {L} layers per turn (same per-layer shapes; the cost is linear in "
+                  f"layers); {args.steps} timed turns after {args.warmup} warm-up")
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_turn * 1e3 * L / CPU_SAMPLE_LAYERS, 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_turn * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": CONFIG,
+            "config": dict(CONFIG, layers_run=CPU_SAMPLE_LAYERS,
+                           step="one turn over the sampled layers: 8 prefix gathers + 1 append"),
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -1045,10 +1087,11 @@ def main():
     e2e = TURN_BYTES * world / (r["e2e_ms"] / args.steps) / 1e6
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, per_turn, threads = cpu_turns(steps=2, warmup=1)
+        gbs, per_turn, threads = cpu_turns(steps=6, warmup=1)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"2 turns (+1 warm-up) over {CPU_SAMPLE_LAYERS} of {L} layers; reference torch ops "
-                         "(index_select / index_copy_) + restated prefix index"}
+               "sample": f"6 turns (+1 warm-up) over {CPU_SAMPLE_LAYERS} of {L} layers; reference torch ops "
+                         "(index_select / index_copy_) + restated prefix index",
+               "ms_per_sample_turn": round(per_turn * 1e3, 3)}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,

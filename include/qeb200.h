@@ -164,6 +164,17 @@ int qe_set_norm_table_mode(int32_t mode);
  * No counterpart in the reference; for measurement and tests. */
 int qe_set_silu_table_mode(int32_t mode);
 
+/* How the fp32 divisions and the reciprocal square root that the reference leaves to its compiler are evaluated
+ * by qe_norm_scale_fp4 / qe_silu_mul_fp4 (process-wide): `1.0 / gs` and `1.0 / (sff * (1.0 / gs))` of the
+ * quantiser (fibo/fp4.py:53-55), `sum / K` and `tl.rsqrt` of the norm (fibo/fp4.py:70). Bits 0-1: the
+ * quantiser's reciprocals, bits 2-3: the norm's mean division (0 = IEEE round-to-nearest, 1 = PTX div.full.f32,
+ * 2 = div.approx.f32, 3 = rcp.approx.f32 then a multiply); bit 4: rsqrt (0 = correctly rounded 1 / sqrt,
+ * 1 = rsqrt.approx.f32). 0 = IEEE everywhere, the rounding of a CPU restatement. The default, 21 = 1 | 1 << 2 |
+ * 1 << 4, reproduces the reference's Triton kernels as Triton compiles them for sm_100 (codes and scales measured
+ * bit-identical on a B200 except for rare row-sum ordering differences of the norm, 2 codes in 100.7 M at
+ * T = 32768). No counterpart in the reference. */
+int qe_set_nvfp4_numerics(int32_t numerics);
+
 /* SiLU kernel load schedule (process-wide): 0 = load then compute (1024 threads per CTA); 1 = the next item's
  * loads issued before the current one is computed (1024 threads; default); 2 = the same with two items per
  * iteration (512 threads). Results are identical. No counterpart in the reference. */

@@ -210,13 +210,40 @@ __device__ __forceinline__ uint32_t absmax16(const uint32_t (&y)[8]) {
   return bamax2(m, __byte_perm(m, 0, 0x1032)) & kAbs2;
 }
 
+// ---- how the reference's fp32 divisions and reciprocal square root are evaluated --------------------------
+// The reference leaves them to the compiler: `1.0 / gs` and `1.0 / (sff * (1.0 / gs))` of the quantiser
+// (fibo/fp4.py:53-55), `sum / K` and `tl.rsqrt` of the norm (fibo/fp4.py:70). `numerics` packs one choice per
+// site: bits 0-1 the quantiser's reciprocals, bits 2-3 the norm's mean division (0 = IEEE round-to-nearest,
+// 1 = div.full.f32, 2 = div.approx.f32, 3 = rcp.approx.f32 then multiply), bits 4-5 the reciprocal square root
+// (0 = 1 / sqrt, both correctly rounded; 1 = rsqrt.approx.f32). 0 everywhere is IEEE arithmetic, the rounding
+// the CPU restatement uses.
+__device__ __forceinline__ float div_sel(float a, float b, int how) {
+  float r;
+  switch (how) {
+    case 1: asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r;
+    case 2: asm("div.approx.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r;
+    case 3: asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(b)); return __fmul_rn(a, r);
+    default: return __fdiv_rn(a, b);
+  }
+}
+__device__ __forceinline__ float rstd_sel(float mean_eps, int how) {
+  if (how == 1) {
+    float r;
+    asm("rsqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(mean_eps));
+    return r;
+  }
+  return __fdiv_rn(1.0f, __fsqrt_rn(mean_eps));
+}
+
 // The reciprocal scale the quantiser multiplies by, for every e4m3 scale byte sb:
 // 1 / (e4m3(sb) * (1 / gs)), or 0 for a zero scale (fibo/fp4.py:53-55). 256 floats, built per CTA.
 constexpr int kScaleTab = 256;
-__device__ __forceinline__ void build_scale_table(float *tab, float inv_gs) {
+__device__ __forceinline__ void build_scale_table(float *tab, float gs, int numerics) {
+  const int how = numerics & 3;
+  const float inv_gs = div_sel(1.0f, gs, how);
   for (int b = threadIdx.x; b < kScaleTab; b += blockDim.x) {
     const float sff = e4m3_value(uint32_t(b));
-    tab[b] = sff != 0.0f ? __frcp_rn(__fmul_rn(sff, inv_gs)) : 0.0f;
+    tab[b] = sff != 0.0f ? div_sel(1.0f, __fmul_rn(sff, inv_gs), how) : 0.0f;
   }
 }
 
@@ -281,6 +308,7 @@ struct NormParams {
   int32_t variants;    // 1, or 2 with a token mask (noisy, clean)
   float eps;
   float *amax;         // amax mode: max |y| over the whole tensor (the calibration pre-pass)
+  int32_t numerics;    // evaluation of the reference's divisions / rsqrt (div_sel, rstd_sel)
 };
 
 // Shared-memory chunk of 16-byte chunk c of a row: leaf-major with an XOR swizzle inside the leaf, chosen so
@@ -428,7 +456,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
   const float kf = float(K);
-  if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
+  if (!kAmax) build_scale_table(scale_tab, gs, p.numerics);
 
   auto fetch = [&](int64_t row, uint4 *dst) {  // issue the async copy of one row (no-op past M)
     if (row < p.M) {
@@ -590,7 +618,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
     const float total = rounds == 1   ? part[0]
                         : rounds == 2 ? __fadd_rn(part[0], part[1])
                                       : __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3]));
-    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, kf), p.eps)));
+    const float rstd = rstd_sel(__fadd_rn(div_sel(total, kf, (p.numerics >> 2) & 3), p.eps), (p.numerics >> 4) & 3);
     const f32x2 rstd2 = pk2(rstd, rstd);
 
     const bool use_noisy = p.mask == nullptr || __ldg(p.mask + s) != 0;
@@ -764,6 +792,14 @@ constexpr int64_t kSiluL1Rows = 1024;
 // load schedule of the SiLU kernel: 0 = load then compute, 1 = pipelined with one item per iteration
 // (1024 threads), 2 = pipelined with two items per iteration (512 threads)
 std::atomic<int> g_silu_pipeline{1};
+// how the reference's fp32 divisions and rsqrt are evaluated (div_sel / rstd_sel bit fields). The default,
+// 1 | 1 << 2 | 1 << 4 (div.full.f32 for the quantiser's reciprocals and the norm's mean, rsqrt.approx.f32), is
+// what reproduces the reference's Triton kernels as this image's Triton compiles them for sm_100: measured on a
+// B200, codes and scales bit-identical on the reference test's shapes and on the benchmark's SiLU shapes (T up to
+// 32768) and norm shapes up to T = 16384; 2 codes of 100.7 M differ at T = 32768 (the row sum's reduction order).
+// 0 (IEEE everywhere) is the rounding of the CPU restatement.
+constexpr int kNumericsTritonGpu = 1 | (1 << 2) | (1 << 4);
+std::atomic<int> g_nvfp4_numerics{kNumericsTritonGpu};
 
 // Row widths with a compile-time specialisation: 3072 (the Fibo / Qwen-Image DiT hidden size); any other
 // multiple of 64 takes the runtime-K kernel.
@@ -803,6 +839,7 @@ struct SiluParams {
   float *amax;  // amax mode: max |y| over the whole tensor (the calibration pre-pass)
   int64_t M, K, padded;
   int32_t wide;  // gate and value are 32-byte aligned: one 256-bit load per lane and tensor
+  int32_t numerics;  // evaluation of the quantiser's reciprocals (div_sel)
 };
 
 constexpr int kSiluThreads = 1024;  // one CTA per SM (the table takes 128 KiB of shared memory)
@@ -837,7 +874,7 @@ __global__ void __launch_bounds__(silu_threads(kSched), 1) silu_mul_fp4_kernel(S
   if (!kL1)
     for (int i = threadIdx.x; i < kSiluTable / 8; i += kThreads) tab4[i] = __ldg(p.table + i);
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
-  if (!kAmax) build_scale_table(scale_tab, __fdiv_rn(1.0f, gs));
+  if (!kAmax) build_scale_table(scale_tab, gs, p.numerics);
   __syncthreads();
   const uint16_t *tab = kL1 ? reinterpret_cast<const uint16_t *>(p.table) : reinterpret_cast<const uint16_t *>(tab4);
   const int lane = threadIdx.x & 31;
@@ -1007,6 +1044,7 @@ int norm_scale_impl(const void *x, const void *w, const void *noisy, const void 
   p.mod_stride = mod_stride;
   p.padded = padded;
   p.eps = eps;
+  p.numerics = qe::g_nvfp4_numerics.load(std::memory_order_relaxed);
   p.amax = amax;
   const int64_t P = qe::next_pow2(K);
   p.leaf_len = P >= 128 ? 128 : int32_t(P);
@@ -1084,6 +1122,13 @@ int qe_set_silu_pipeline(int32_t on) {
   return qe::ok();
 }
 
+int qe_set_nvfp4_numerics(int32_t numerics) {
+  if (numerics < 0 || numerics > 0x1f)
+    return fail(QE_ERR_INVALID, "qe_set_nvfp4_numerics: bits 0-1 and 2-3 in 0..3, bit 4 in 0..1");
+  qe::g_nvfp4_numerics.store(numerics, std::memory_order_relaxed);
+  return qe::ok();
+}
+
 int qe_set_norm_table_mode(int32_t mode) {
   if (mode < 0 || mode > 2) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0, 1 or 2");
   qe::g_norm_table_mode.store(mode, std::memory_order_relaxed);
@@ -1133,6 +1178,7 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   p.K = K;
   p.padded = padded;
   p.wide = ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(value)) & 31) == 0 ? 1 : 0;
+  p.numerics = qe::g_nvfp4_numerics.load(std::memory_order_relaxed);
   const int mode = g_silu_table_mode.load(std::memory_order_relaxed);
   const bool l1 = mode == 2 || (mode == 0 && M < kSiluL1Rows);
   const int sched = g_silu_pipeline.load(std::memory_order_relaxed);

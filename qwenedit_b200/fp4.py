@@ -11,6 +11,10 @@ Each call is one launch of a hand-written sm_100a kernel from libqeb200 on the c
 adaLN modulation rows may be strided column slices of one [B, 4K] tensor, as in the reference
 (``noisy.stride(0)``, fp4.py:106). ``shift`` / ``shift_clean`` (optional, not in the reference) add an adaLN
 shift after the scale: ``bf16(bf16(y * bf16(1 + scale)) + shift)``.
+
+``set_numerics`` picks how the fp32 divisions and the rsqrt the reference leaves to its compiler are evaluated:
+"triton" (the default) as the reference's Triton kernels compile for sm_100 (div.full.f32, rsqrt.approx.f32:
+bit-identical to them on the B200), "ieee" with correctly rounded operations (the CPU restatement's rounding).
 """
 
 from __future__ import annotations
@@ -20,6 +24,15 @@ from typing import NamedTuple
 import torch
 
 from qwenedit_b200 import _lib
+
+
+NUMERICS = {"ieee": 0, "triton": 1 | (1 << 2) | (1 << 4)}
+
+
+def set_numerics(mode: str | int) -> None:
+    """Process-wide evaluation of the quantisers' divisions and rsqrt ("triton" default, "ieee", or the raw bit
+    field of qe_set_nvfp4_numerics)."""
+    _lib.call("qe_set_nvfp4_numerics", NUMERICS[mode] if isinstance(mode, str) else int(mode))
 
 
 class Quantized(NamedTuple):

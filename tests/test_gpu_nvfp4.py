@@ -3,7 +3,9 @@
 shapes, the reference test's shapes (tests/test_fibo_fp4.py:39-58) and edge cases.
 
 Tolerance (stated by the build's spec for NVFP4): bit-exact codes and scales, or <= 1 code step on <= 1e-4 of
-elements with the dequantised max-abs error reported. These tests require bit-exact."""
+elements with the dequantised max-abs error reported. These tests require bit-exact, with the kernels in their
+IEEE numerics (correctly rounded divisions and rsqrt, the rounding the oracle and the golden outputs use); the
+default "triton" numerics is compared with the reference's kernels on the GPU in test_gpu_nvfp4_triton.py."""
 
 import functools
 import json
@@ -22,6 +24,16 @@ from tests.golden import cases, inputs
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(autouse=True, scope="module")
+def ieee_numerics():
+    """The oracle and the golden outputs round every division and the rsqrt correctly (IEEE)."""
+    from qwenedit_b200.fp4 import set_numerics
+
+    set_numerics("ieee")
+    yield
+    set_numerics("triton")
 
 
 @pytest.fixture(scope="module")
@@ -137,6 +149,42 @@ def test_norm_scale_k3072_tmem_layouts(B, masked, shift, table_mode):
     to = lambda t: None if t is None else t.to(DEV)  # noqa: E731
     out = norm_scale_fp4(to(x), SimpleNamespace(weight=to(w), eps=1e-6), to(scale), to(clean), to(mask), _gs(gs),
                          shift=to(sh), shift_clean=to(sh_clean))
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@pytest.mark.parametrize("masked,shift", [(False, False), (False, True), (True, True)])
+def test_norm_scale_full_benchmark_size(masked, shift):
+    """The largest benchmark NVFP4 shape, x [1, 32768, 3072] (eps 1e-6, w ~ 1 + 0.02 N, scale / shift ~ 0.1 N),
+    plain, with an adaLN shift, and with a token mask selecting noisy / clean rows: bit-exact to the oracle."""
+    K, S, seed = 3072, 32768, 500 + 2 * masked + shift
+    x = torch.randn(1, S, K, generator=torch.Generator().manual_seed(seed)).bfloat16()
+    w = inputs.bf16(seed + 1, (K,), scale=0.02, shift=1.0)
+    scale = inputs.bf16(seed + 2, (1, K), scale=0.1)
+    clean = inputs.bf16(seed + 3, (1, K), scale=0.1) if masked else None
+    mask = torch.from_numpy(inputs.uniforms(seed + 4, S) < 0.5) if masked else None
+    sh = inputs.bf16(seed + 5, (1, K), scale=0.1) if shift else None
+    sh_clean = inputs.bf16(seed + 6, (1, K), scale=0.1) if (shift and masked) else None
+    gs = nvfp4_ref.global_scale(nvfp4_ref.bf16_values_norm_scale(x, w, 1e-6, scale, clean, mask, sh, sh_clean))
+    q_ref, sf_ref = nvfp4_ref.norm_scale_fp4_ref(x, w, 1e-6, scale, clean, mask, gs, sh, sh_clean)
+    to = lambda t: None if t is None else t.to(DEV)  # noqa: E731
+    out = norm_scale_fp4(to(x), SimpleNamespace(weight=to(w), eps=1e-6), to(scale), to(clean), to(mask), _gs(gs),
+                         shift=to(sh), shift_clean=to(sh_clean))
+    np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
+
+
+@pytest.mark.parametrize("M", [16384, 32768])
+def test_silu_mul_full_benchmark_sizes(M):
+    """SiLU * mul at the benchmark's [M, 12288] shapes, bit-exact to the oracle (default table home and
+    schedule for these sizes)."""
+    K = 12288
+    gen = torch.Generator().manual_seed(M)
+    gate = torch.randn(1, M, K, generator=gen).bfloat16()
+    value = torch.randn(1, M, K, generator=gen).bfloat16()
+    gs = 7.5  # inside the calibrated range for N(0, 1) inputs (amax of silu(g) * v is about 20)
+    q_ref, sf_ref = nvfp4_ref.silu_mul_fp4_ref(gate, value, gs)
+    out = silu_mul_fp4(gate.to(DEV), value.to(DEV), _gs(gs))
     np.testing.assert_array_equal(out.q.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(out.sf.cpu().numpy(), sf_ref)
 

@@ -137,3 +137,14 @@ def test_scatter_append_checks_its_geometry_first():
     scatter("planes_inner", src=_lib.planes(A, 0, 0, 0))
     scatter("multiples of 16 bytes", pool=_lib.planes(A, 24, 0, 1))
     scatter("source must be 16-byte aligned", src=_lib.planes(A + 8, 0, 0, 1))
+
+
+def test_nvfp4_numerics_setter_checks_its_fields():
+    from qwenedit_b200.fp4 import NUMERICS, set_numerics
+
+    for bad in (-1, 0x20, 0x40):
+        with pytest.raises(ValueError, match="qe_set_nvfp4_numerics"):
+            set_numerics(bad)
+    assert NUMERICS == {"ieee": 0, "triton": 21}
+    set_numerics("ieee")
+    set_numerics("triton")  # the default, restored
