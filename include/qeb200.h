@@ -202,6 +202,34 @@ int qe_norm_scale_amax(const void *x, const void *w, const void *noisy, const vo
 int qe_silu_mul_amax(const void *gate, const void *value, int64_t M, int64_t K, const uint16_t *silu_table,
                      float *amax, void *stream);
 
+/* ---- paged joint attention (device) ----------------------------------------------------------
+ *
+ * out = softmax(scale * q K^T) V, K / V = [the first n_prefix tokens of a prefix held in pool pages; n_local own
+ * tokens], in one launch that reads the prefix K/V tiles from the pool through the block table (TMA tile loads)
+ * and runs both products on the tensor cores (tcgen05, fp32 accumulation). Replaces the per-step gather of the
+ * matched prefix (multi_turn/pipeline/hooks.py:101-105 -> cache/paged.py:106-113) that feeds the DiT's joint
+ * attention through the per-layer caches (hooks.py:81-83), and the text encoder's partial-hit attention over
+ * [gathered prefix; tail] (cache/encoder.py:173-190: grouped-query heads, causal tail).
+ *   q        bf16 [n_q][heads_q][128]: element (i, h, d) at q + i * q_token_stride + h * q_head_stride (bytes)
+ *   k_pool / v_pool  the layer's K and V planes of the pool: rows of heads_kv x 128 bf16, row r at
+ *            plane + r * heads_kv * 256; pool_rows = rows of a plane (a multiple of page_size)
+ *   block_table  device int32 page ids, ceil(n_prefix / page_size) of them; prefix token t is pool row
+ *            block_table[t / page_size] * page_size + t % page_size. page_size: 8, 16, 32, 64 or 128, or a
+ *            multiple of 128. Pages outside the pool read as zeros and set bit 1 of *err_flag.
+ *   k_local / v_local  bf16 [n_local][heads_kv][128] with the given strides (may be null when n_local == 0)
+ *   causal   query i sees every prefix token and own tokens j <= i + n_local - n_q (bottom-right alignment)
+ *   heads_q  a multiple of heads_kv (query head h reads K/V head h / (heads_q / heads_kv))
+ *   out      bf16 [n_q][heads_q][128] (strides in bytes); lse (optional) fp32 [heads_q][n_q]: the natural log of
+ *            the softmax denominator of the scaled scores.
+ * Everything 16-byte aligned with 16-byte multiple strides. Every internal wait is bounded; a wait that gives up
+ * sets bit 2 of *err_flag. No counterpart as one operation in the reference (gather + the model's attention). */
+int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q, int32_t heads_q,
+                       const void *k_pool, const void *v_pool, int64_t pool_rows, int32_t heads_kv,
+                       const int32_t *block_table, int32_t page_size, int32_t n_prefix, const void *k_local,
+                       const void *v_local, int64_t local_token_stride, int64_t local_head_stride, int32_t n_local,
+                       int32_t causal, float scale, void *out, int64_t out_token_stride, int64_t out_head_stride,
+                       float *lse, int32_t *err_flag, void *stream);
+
 /* ---- head-sharded pools across the GPUs of one node ------------------------------------------
  *
  * No counterpart in the reference, which keeps a prefix on one GPU and disables the pool under tensor or

@@ -65,6 +65,9 @@ SIGNATURES: dict[str, list] = {
     "qe_set_silu_table_mode": [c_int32],
     "qe_set_silu_pipeline": [c_int32],
     "qe_set_nvfp4_numerics": [c_int32],
+    "qe_paged_attention": [c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int32,
+                           c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
+                           c_float, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "qe_norm_scale_amax": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p],
     "qe_silu_mul_amax": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],

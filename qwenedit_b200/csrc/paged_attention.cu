@@ -1,0 +1,637 @@
+// Paged joint attention: attention of a block of queries over the cached prefix K/V, read straight from the
+// prefix pool through the block table, together with the step's own K/V, in one kernel.
+//
+// Replaces, for the DiT prefix cache, the per-step materialisation the reference does before its attention:
+// multi_turn/pipeline/hooks.py:101-105 gathers the matched prefix (PagedKVPool.gather, cache/paged.py:106-113,
+// kv.index_select of 2 * L * H * D values per token) and hooks.py:81-83 hands the per-layer K/V views to the
+// model's joint attention, which concatenates them with the step's own K/V. Here the attention reads the K/V tiles
+// from the pool pages themselves (TMA tile loads addressed by the block table) and no gathered copy exists.
+// The same kernel covers the text encoder's partial hit (cache/encoder.py:173-190): grouped-query heads and a
+// bottom-right causal mask on the step's own (tail) keys.
+//
+// Per CTA: two 128-query tiles of one query head (M = 256), head_dim 128, bf16 in, fp32 accumulation, bf16 out.
+//   warp 8       TMA producer: the Q tiles once, then per 128-key tile the K tile and the V tile into a
+//                two-stage ring each (pool pages: 4-D tensor maps [D, H, row-in-page, page] of the K or V plane of
+//                the layer; the step's own keys: 3-D maps [D, H, token])
+//   warp 9       tcgen05.mma issuer (one thread) and owner of the 512 tensor-memory columns:
+//                S_t = Q_t K^T (SS form, both operands K-major in 128-byte swizzled shared memory) and
+//                O_t += P_t V (TS form: P_t from tensor memory, V MN-major in shared memory)
+//   warps 0-7    softmax, one warpgroup per Q tile, one thread per query row (tensor-memory lane = row):
+//                S row from tensor memory, masking, online max with a lazy rescale of O (only when the max
+//                grows by more than 2^8), exp2, row sum, P written back over S as bf16, and the epilogue
+//                O / l -> bf16 (+ log-sum-exp)
+// Tensor memory: S0 | O0 | S1 | O1, 128 fp32 columns each; P_t (bf16 pairs) overwrites the first 64 columns of S_t.
+// The MMAs of one thread execute in issue order, so PV_t(j) reads P_t(j) before QK_t(j+1) rewrites S_t.
+// Every mbarrier wait is bounded (kWaitNs); on expiry the CTA records QE_ERR_TIMEOUT in the error flag (bit 2),
+// drains what it issued and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "qe_cuda.cuh"
+
+namespace qe {
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kTile = 128;                       // queries per Q tile, keys per K/V tile
+constexpr int kQTiles = 2;                       // Q tiles per CTA
+constexpr int kTileBytes = kTile * kHeadDim * 2;  // 32 KiB: one Q, K or V tile
+constexpr int kHalfBytes = kTileBytes / 2;        // 16 KiB: 128 rows x 64 dims, one 128-byte swizzle span per row
+constexpr int kThreads = 320;                     // 8 softmax warps, the producer, the MMA warp
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the running max grows by more than this (log2 units)
+
+// shared memory, from a 1024-byte aligned base
+constexpr int kQOff = 0;
+constexpr int kKOff = kQOff + kQTiles * kTileBytes;  // 2 stages
+constexpr int kVOff = kKOff + 2 * kTileBytes;        // 2 stages
+constexpr int kBarOff = kVOff + 2 * kTileBytes;
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPReady = 11, kOFinal = 13,
+           kDrain = 14, kNumBars = 15 };
+constexpr int kSlotOff = kBarOff + kNumBars * 8;  // tensor-memory base address
+constexpr int kAbortOff = kSlotOff + 4;
+constexpr int kSmemBytes = kAbortOff + 4 + 1024;  // + slack to align the base
+
+struct AttnParams {
+  const int32_t *block_table;
+  int32_t page_size, n_prefix, prefix_tiles, pool_pages, last_page, tail_rows;
+  int32_t n_q, n_local, heads_q, group, causal;
+  float scale_log2;
+  __nv_bfloat16 *out;
+  int64_t out_token_stride, out_head_stride;  // elements
+  float *lse;
+  int32_t *err;
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the phase of `parity` to complete. Gives up (false) after kWaitNs or once another role of the
+// CTA has given up; the first to give up records the timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int32_t *err) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try(bar, parity)) return true;
+    if ((spin & 255u) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        *abort = 1;
+        if (err) atomicOr(err, 2);
+        return false;
+      }
+    }
+  }
+}
+
+// ---- TMA ----------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// ---- tcgen05 ------------------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor, 128-byte swizzle: start address, leading / stride byte offsets (16-byte
+// units), descriptor version 1 (bits 46-47), layout type 2 = SWIZZLE_128B (bits 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((addr >> 4) & 0x3fffu) | (uint64_t((lbo >> 4) & 0x3fffu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3fffu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bit 4), bf16 A (bits 7-9 = 1) and B (bits 10-12 = 1),
+// A K-major, B K-major (QK) or MN-major (PV, bit 16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTile >> 3) << 17) |
+                              (uint32_t(kTile >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's lane, waited for inside the statement (no register is read early)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__global__ void __maxnreg__(200)
+    paged_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kpool,
+                           const __grid_constant__ CUtensorMap tm_vpool, const __grid_constant__ CUtensorMap tm_ktail,
+                           const __grid_constant__ CUtensorMap tm_vtail, const __grid_constant__ CUtensorMap tm_klocal,
+                           const __grid_constant__ CUtensorMap tm_vlocal, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bars = sbase + kBarOff;
+  auto bar = [&](int i) { return bars + 8u * uint32_t(i); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kSlotOff);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + kAbortOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int q0 = blockIdx.x * (kQTiles * kTile);
+  const int hq = blockIdx.y;
+  const int hkv = hq / p.group;
+  // key tiles: the prefix's, then the visible ones of the step's own keys
+  int local_tiles = 0;
+  if (p.n_local > 0) {
+    int last_key = p.n_local - 1;
+    if (p.causal) last_key = min(last_key, min(q0 + kQTiles * kTile, p.n_q) - 1 + p.n_local - p.n_q);
+    local_tiles = last_key >= 0 ? last_key / kTile + 1 : 0;
+  }
+  const int n_tiles = p.prefix_tiles + local_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kQFull), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(kKFull + s), 1);
+      mbar_init(bar(kKEmpty + s), 1);
+      mbar_init(bar(kVFull + s), 1);
+      mbar_init(bar(kVEmpty + s), 1);
+      mbar_init(bar(kSFull + s), 1);
+      mbar_init(bar(kPReady + s), kTile);
+    }
+    mbar_init(bar(kOFinal), 1);
+    mbar_init(bar(kDrain), 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      // ---- producer: Q once, then K_j and V_j through two-stage rings ----
+      mbar_expect_tx(bar(kQFull), kQTiles * kTileBytes);
+      for (int t = 0; t < kQTiles; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sbase + kQOff + t * kTileBytes + h * kHalfBytes, &tm_q, h * 64, hq, q0 + t * kTile, bar(kQFull));
+      const int P = p.page_size;
+      auto load_tile = [&](int it, uint32_t dst, bool is_v, uint32_t full) {
+        if (it < p.prefix_tiles) {
+          const CUtensorMap *full_map = is_v ? &tm_vpool : &tm_kpool;
+          const CUtensorMap *tail_map = is_v ? &tm_vtail : &tm_ktail;
+          const int k0 = it * kTile;
+          if (P >= kTile) {  // the tile lies inside one page
+            const int pi = k0 / P;
+            int page = __ldg(p.block_table + pi);
+            if (page < 0 || page >= p.pool_pages) {
+              if (p.err) atomicOr(p.err, 1);
+              page = p.pool_pages;  // out of the map: the copy reads zeros
+            }
+            const CUtensorMap *map = pi == p.last_page ? tail_map : full_map;
+            for (int h = 0; h < 2; ++h) tma_load_4d(dst + h * kHalfBytes, map, h * 64, hkv, k0 % P, page, full);
+          } else {  // kTile / P pages per tile
+            for (int sub = 0; sub < kTile / P; ++sub) {
+              const int key = k0 + sub * P;
+              const int pi = key / P;
+              int page = p.pool_pages;  // past the prefix: zeros
+              const CUtensorMap *map = full_map;
+              if (key < p.n_prefix) {
+                page = __ldg(p.block_table + pi);
+                if (page < 0 || page >= p.pool_pages) {
+                  if (p.err) atomicOr(p.err, 1);
+                  page = p.pool_pages;
+                }
+                if (pi == p.last_page) map = tail_map;
+              }
+              for (int h = 0; h < 2; ++h)
+                tma_load_4d(dst + h * kHalfBytes + sub * P * 128, map, h * 64, hkv, 0, page, full);
+            }
+          }
+        } else {
+          const int l0 = (it - p.prefix_tiles) * kTile;
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(dst + h * kHalfBytes, is_v ? &tm_vlocal : &tm_klocal, h * 64, hkv, l0, full);
+        }
+      };
+      bool ok = true;
+      for (int it = 0; it < n_tiles && ok; ++it) {
+        const int s = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        ok = mbar_wait(bar(kKEmpty + s), ph ^ 1, abort, p.err);
+        if (!ok) break;
+        mbar_expect_tx(bar(kKFull + s), kTileBytes);
+        load_tile(it, sbase + kKOff + s * kTileBytes, false, bar(kKFull + s));
+        ok = mbar_wait(bar(kVEmpty + s), ph ^ 1, abort, p.err);
+        if (!ok) break;
+        mbar_expect_tx(bar(kVFull + s), kTileBytes);
+        load_tile(it, sbase + kVOff + s * kTileBytes, true, bar(kVFull + s));
+      }
+      if (!ok) {  // give the copies already issued time to land before the CTA's shared memory is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      const uint32_t q_addr = sbase + kQOff, k_addr = sbase + kKOff, v_addr = sbase + kVOff;
+      auto qk = [&](int t, int ks) {  // S_t = Q_t K^T over the 128 head dims, 8 steps of 16
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = uint32_t((k >> 2) * kHalfBytes + (k & 3) * 32);
+          mma_ss(tmem + t * 256, sw128_desc(q_addr + t * kTileBytes + off, 16, 1024),
+                 sw128_desc(k_addr + ks * kTileBytes + off, 16, 1024), kIdescQK, k > 0);
+        }
+      };
+      auto pv = [&](int t, int vs, bool acc) {  // O_t += P_t V over 128 keys, 8 steps of 16
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k,
+                 sw128_desc(v_addr + vs * kTileBytes + k * 2048, kHalfBytes, 1024), kIdescPV, acc || k > 0);
+      };
+      bool ok = mbar_wait(bar(kQFull), 0, abort, p.err);
+      if (ok && n_tiles > 0) {
+        ok = mbar_wait(bar(kKFull), 0, abort, p.err);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < kQTiles; ++t) {
+            qk(t, 0);
+            mma_commit(bar(kSFull + t));
+          }
+          mma_commit(bar(kKEmpty));
+        }
+        for (int it = 0; it < n_tiles && ok; ++it) {
+          const int s = it & 1;
+          ok = mbar_wait(bar(kVFull + s), (it >> 1) & 1, abort, p.err);
+          if (!ok) break;
+          const int s1 = (it + 1) & 1;
+          for (int t = 0; t < kQTiles && ok; ++t) {
+            ok = mbar_wait(bar(kPReady + t), it & 1, abort, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            pv(t, s, it > 0);
+            if (it + 1 < n_tiles) {
+              if (t == 0) {
+                ok = mbar_wait(bar(kKFull + s1), ((it + 1) >> 1) & 1, abort, p.err);
+                if (!ok) break;
+                tc_fence_after();
+              }
+              qk(t, s1);
+              mma_commit(bar(kSFull + t));
+            }
+          }
+          if (!ok) break;
+          mma_commit(bar(kVEmpty + s));
+          if (it + 1 < n_tiles) mma_commit(bar(kKEmpty + s1));
+        }
+      }
+      mma_commit(bar(kOFinal));
+      if (!ok) {  // wait (bounded) for the MMAs already issued before the tensor memory is released
+        mma_commit(bar(kDrain));
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(bar(kDrain), 0) && globaltimer() - t0 < kWaitNs) {
+        }
+      }
+    }
+  } else {
+    // ---- softmax warpgroups: warp w handles tile w / 4, tensor-memory lanes 32 (w % 4) .. + 31 ----
+    const int t = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const int qi = q0 + t * kTile + row;
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const uint32_t s_col = lane_base + t * 256, o_col = s_col + 128;
+    const int causal_shift = p.n_local - p.n_q;  // query i sees own keys j <= i + causal_shift
+    float m_use = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int it = 0; it < n_tiles; ++it) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kSFull + t), it & 1, abort, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      // visible keys of this tile: [0, limit)
+      int limit;
+      if (it < p.prefix_tiles) {
+        limit = p.n_prefix - it * kTile;
+      } else {
+        const int l0 = (it - p.prefix_tiles) * kTile;
+        limit = p.n_local - l0;
+        if (p.causal) limit = min(limit, qi + causal_shift - l0 + 1);
+      }
+      float s[kTile];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float chunk[32];
+        tmem_ld32(s_col + 32 * c, chunk);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 * c + i] = chunk[i];
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTile; ++c) {
+        s[c] = c < limit ? s[c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      // A row moves its reference max only when its max grew by more than 2^8 (also when m_use is still -inf and
+      // a key is visible); its O (earlier tiles' sums at the old max) is scaled down to match. The tensor-memory
+      // accesses are warp-collective, so a warp rescales together: rows that keep their max scale by 1.
+      const bool grow = mx > m_use + kRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float f = grow && m_use != -INFINITY ? ex2(m_use - mx) : 1.0f;
+        if (it > 0) {  // before the first P V, O holds nothing yet
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            uint32_t w[32];
+            tmem_ld32(o_col + 32 * c, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * f);
+            tmem_st32(o_col + 32 * c, w);
+          }
+        }
+        l *= f;
+        if (grow) m_use = mx;
+      }
+      const float base = m_use == -INFINITY ? 0.0f : m_use;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = ex2(s[64 * h + 2 * i] - base), b = ex2(s[64 * h + 2 * i + 1] - base);
+          l += a + b;
+          w[i] = pack_bf16(a, b);
+        }
+        tmem_st32(s_col + 32 * h, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kPReady + t));
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(kOFinal), 0, abort, p.err));
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      const bool store = qi < p.n_q;
+      __nv_bfloat16 *dst = p.out + int64_t(qi) * p.out_token_stride + int64_t(hq) * p.out_head_stride;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tmem_ld32(o_col + 32 * c, o);  // warp-collective: every lane loads, only valid rows store
+        if (l == 0.0f) {  // a row that saw no key: zeros (its O columns were never written)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.0f;
+        }
+        if (store) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 pk;
+            pk.x = pack_bf16(o[8 * v + 0] * inv, o[8 * v + 1] * inv);
+            pk.y = pack_bf16(o[8 * v + 2] * inv, o[8 * v + 3] * inv);
+            pk.z = pack_bf16(o[8 * v + 4] * inv, o[8 * v + 5] * inv);
+            pk.w = pack_bf16(o[8 * v + 6] * inv, o[8 * v + 7] * inv);
+            *reinterpret_cast<uint4 *>(dst + 32 * c + 8 * v) = pk;
+          }
+        }
+      }
+      if (store && p.lse) {
+        const float ln2 = 0.69314718055994530942f;
+        p.lse[int64_t(hq) * p.n_q + qi] = l > 0.0f ? (m_use + __log2f(l)) * ln2 : -INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---- host ---------------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// bf16 tensor map with a 128-byte swizzle; dims / strides innermost first (strides of dims 1.. in bytes)
+int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+             const uint32_t *box, const char *what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(QE_ERR_CUDA, "qe_paged_attention: cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void *>(base),
+                  reinterpret_cast<const cuuint64_t *>(dims), reinterpret_cast<const cuuint64_t *>(strides),
+                  reinterpret_cast<const cuuint32_t *>(box), elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QE_ERR_INVALID, "qe_paged_attention: tensor map for %s rejected (%d)", what, int(r));
+  return QE_OK;
+}
+
+bool al16(int64_t v) { return v % 16 == 0; }
+
+}  // namespace
+}  // namespace qe
+
+using qe::fail;
+
+extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,
+                                  int32_t heads_q, const void *k_pool, const void *v_pool, int64_t pool_rows,
+                                  int32_t heads_kv, const int32_t *block_table, int32_t page_size, int32_t n_prefix,
+                                  const void *k_local, const void *v_local, int64_t local_token_stride,
+                                  int64_t local_head_stride, int32_t n_local, int32_t causal, float scale, void *out,
+                                  int64_t out_token_stride, int64_t out_head_stride, float *lse, int32_t *err_flag,
+                                  void *stream) {
+  using namespace qe;
+  QE_CHECK_ARG(n_q >= 0 && n_prefix >= 0 && n_local >= 0, "qe_paged_attention: negative size");
+  QE_CHECK_ARG(heads_q >= 1 && heads_kv >= 1 && heads_q % heads_kv == 0 && heads_q <= 65535,
+               "qe_paged_attention: heads_q must be a positive multiple of heads_kv (at most 65535)");
+  if (n_q == 0) return ok();
+  QE_CHECK_ARG(q && out, "qe_paged_attention: null q or out");
+  QE_CHECK_ARG(n_prefix + n_local >= 1, "qe_paged_attention: no keys (n_prefix + n_local == 0)");
+  QE_CHECK_ARG(aligned16(q) && aligned16(out) && al16(q_token_stride) && al16(q_head_stride) &&
+                   al16(out_token_stride) && al16(out_head_stride) && q_head_stride >= 256 &&
+                   out_head_stride >= 256 && q_token_stride > 0 && out_token_stride > 0,
+               "qe_paged_attention: q / out must be 16-byte aligned with 16-byte multiple strides, rows of 128 bf16");
+  QE_CHECK_ARG(std::isfinite(scale) && scale > 0.0f, "qe_paged_attention: scale must be positive and finite");
+  int32_t prefix_tiles = 0, pool_pages = 0, last_page = -1, tail_rows = 0;
+  if (n_prefix > 0) {
+    QE_CHECK_ARG(k_pool && v_pool && block_table, "qe_paged_attention: null pool plane or block table");
+    QE_CHECK_ARG(aligned16(k_pool) && aligned16(v_pool), "qe_paged_attention: pool planes must be 16-byte aligned");
+    QE_CHECK_ARG(page_size >= 8 && ((kTile % page_size) == 0 || (page_size % kTile) == 0) && page_size <= 1 << 20,
+                 "qe_paged_attention: page_size must be a divisor of 128 (>= 8) or a multiple of 128");
+    QE_CHECK_ARG(pool_rows >= page_size && pool_rows % page_size == 0 && pool_rows / page_size < (int64_t(1) << 31),
+                 "qe_paged_attention: pool_rows must be a positive multiple of page_size");
+    prefix_tiles = (n_prefix + kTile - 1) / kTile;
+    pool_pages = int32_t(pool_rows / page_size);
+    last_page = (n_prefix - 1) / page_size;
+    tail_rows = n_prefix - last_page * page_size;
+  }
+  if (n_local > 0) {
+    QE_CHECK_ARG(k_local && v_local && aligned16(k_local) && aligned16(v_local) && al16(local_token_stride) &&
+                     al16(local_head_stride) && local_token_stride > 0 && local_head_stride >= 256,
+                 "qe_paged_attention: local K / V must be 16-byte aligned with 16-byte multiple strides");
+  }
+  CUtensorMap maps[7];
+  std::memset(maps, 0, sizeof(maps));
+  const uint32_t box3[3] = {64, 1, uint32_t(kTile)};
+  int s;
+  {
+    const uint64_t dims[3] = {uint64_t(kHeadDim), uint64_t(heads_q), uint64_t(n_q)};
+    const uint64_t strides[2] = {uint64_t(q_head_stride), uint64_t(q_token_stride)};
+    if ((s = make_map(&maps[0], q, 3, dims, strides, box3, "q"))) return s;
+  }
+  const int64_t row_bytes = int64_t(heads_kv) * kHeadDim * 2;
+  if (n_prefix > 0) {
+    const uint32_t box_rows = uint32_t(std::min(page_size, kTile));
+    const uint32_t box4[4] = {64, 1, box_rows, 1};
+    const uint64_t strides[3] = {uint64_t(kHeadDim * 2), uint64_t(row_bytes), uint64_t(row_bytes * page_size)};
+    const uint64_t full[4] = {uint64_t(kHeadDim), uint64_t(heads_kv), uint64_t(page_size), uint64_t(pool_pages)};
+    const uint64_t tail[4] = {uint64_t(kHeadDim), uint64_t(heads_kv), uint64_t(tail_rows), uint64_t(pool_pages)};
+    if ((s = make_map(&maps[1], k_pool, 4, full, strides, box4, "the K pool"))) return s;
+    if ((s = make_map(&maps[2], v_pool, 4, full, strides, box4, "the V pool"))) return s;
+    if ((s = make_map(&maps[3], k_pool, 4, tail, strides, box4, "the K pool tail"))) return s;
+    if ((s = make_map(&maps[4], v_pool, 4, tail, strides, box4, "the V pool tail"))) return s;
+  }
+  if (n_local > 0) {
+    const uint64_t dims[3] = {uint64_t(kHeadDim), uint64_t(heads_kv), uint64_t(n_local)};
+    const uint64_t strides[2] = {uint64_t(local_head_stride), uint64_t(local_token_stride)};
+    if ((s = make_map(&maps[5], k_local, 3, dims, strides, box3, "local K"))) return s;
+    if ((s = make_map(&maps[6], v_local, 3, dims, strides, box3, "local V"))) return s;
+  }
+  AttnParams p{};
+  p.block_table = block_table;
+  p.page_size = page_size;
+  p.n_prefix = n_prefix;
+  p.prefix_tiles = prefix_tiles;
+  p.pool_pages = pool_pages;
+  p.last_page = last_page;
+  p.tail_rows = tail_rows;
+  p.n_q = n_q;
+  p.n_local = n_local;
+  p.heads_q = heads_q;
+  p.group = heads_q / heads_kv;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.44269504088896341f;
+  p.out = static_cast<__nv_bfloat16 *>(out);
+  p.out_token_stride = out_token_stride / 2;
+  p.out_head_stride = out_head_stride / 2;
+  p.lse = lse;
+  p.err = err_flag;
+
+  static std::atomic<bool> attr_done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!attr_done[dev].load(std::memory_order_relaxed)) {
+    cudaError_t e = cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "qe_paged_attention: smem attribute");
+    attr_done[dev].store(true, std::memory_order_relaxed);
+  }
+  const dim3 grid(unsigned((n_q + kQTiles * kTile - 1) / (kQTiles * kTile)), unsigned(heads_q));
+  paged_attention_kernel<<<grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+      maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], p);
+  s = cuda_status(cudaGetLastError(), "qe_paged_attention launch");
+  return s ? s : ok();
+}

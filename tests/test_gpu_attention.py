@@ -1,0 +1,184 @@
+"""Paged joint attention (qe_paged_attention) against an fp32 PyTorch attention over the gathered prefix.
+
+The reference path gathers the matched prefix (PagedKVPool.gather, cache/paged.py:106-113) and attends over
+[prefix; the step's own K/V] (the DiT's joint attention fed by pipeline/hooks.py:81-83; the encoder tail's SDPA,
+cache/encoder.py:173-190, with grouped-query heads and a bottom-right causal mask). The kernel reads the prefix
+straight from the pool pages. Every pool row that is not part of the prefix (other pages, and the rows of the
+last page past the prefix) holds NaN, so reading one would poison the output.
+
+Tolerance: the kernel takes bf16 inputs, accumulates in fp32 and rounds P to bf16 before P V, and its output is
+bf16: |out - ref| <= 1e-2 + 2e-2 |ref| elementwise against fp32 math on the same bf16 inputs, and the mean
+absolute error below 2e-3; the log-sum-exp within 1e-3.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from qwenedit_b200.attention import PagedPrefix, paged_attention
+from qwenedit_b200.paged import PagedKVPool
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+D = 128
+
+
+def _pool(layers, heads, page, n_pages, seed):
+    """A page-mode pool of n_pages pages filled with NaN."""
+    budget = n_pages * page * layers * 2 * heads * D * 2
+    pool = PagedKVPool("attn", layers, heads, D, budget, torch.bfloat16, DEV, page_size=page)
+    pool.kv.fill_(float("nan"))
+    return pool
+
+
+def _prefix(pool, n, seed):
+    """Scattered pages for an n-token prefix, their rows filled with N(0, 1) values; the rest stays NaN."""
+    P = pool.page_size
+    rng = np.random.default_rng(seed)
+    pages = rng.permutation(np.arange(1, pool.rows // P))[: -(-n // P)]
+    t = np.arange(n)
+    slots = torch.from_numpy(pages[t // P] * P + t % P).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    vals = torch.randn(pool.layers, 2, n, pool.heads, D, generator=g, device=DEV).bfloat16()
+    pool.kv[:, :, slots] = vals
+    return slots, vals
+
+
+def _reference(q, k, v, scale, causal, n_local):
+    """fp32 attention, q [n_q, Hq, D], k / v [n_k, Hkv, D] (prefix then own); returns out [n_q, Hq, D], lse."""
+    n_q, hq = q.shape[:2]
+    group = hq // k.shape[1]
+    qf = q.float().transpose(0, 1)
+    kf = k.float().transpose(0, 1).repeat_interleave(group, 0)
+    vf = v.float().transpose(0, 1).repeat_interleave(group, 0)
+    s = qf @ kf.transpose(1, 2) * scale
+    if causal:
+        n_k = k.shape[0]
+        n_pre = n_k - n_local
+        i = torch.arange(n_q, device=q.device)[:, None]
+        j = torch.arange(n_k, device=q.device)[None, :]
+        visible = (j < n_pre) | (j - n_pre <= i + n_local - n_q)
+        s = s.masked_fill(~visible, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    out = torch.softmax(s, dim=-1) @ vf
+    return out.transpose(0, 1), lse
+
+
+def _check(out, lse, ref_out, ref_lse):
+    assert not torch.isnan(out).any(), "NaN in the output: a row outside the prefix was read"
+    err = (out.float() - ref_out).abs()
+    assert bool((err <= 1e-2 + 2e-2 * ref_out.abs()).all()), f"max abs error {err.max().item()}"
+    assert err.mean().item() < 2e-3, err.mean().item()
+    if lse is not None:
+        assert torch.allclose(lse, ref_lse, atol=1e-3, rtol=1e-4), (lse - ref_lse).abs().max().item()
+
+
+CASES = [  # (page, heads_q, heads_kv, n_q, n_prefix, n_local, causal, layers, layer)
+    (64, 4, 4, 300, 1000, 0, False, 2, 1),      # partial Q tiles, partial last page, prefix only
+    (64, 2, 2, 512, 4608, 512, False, 1, 0),    # the DiT's joint attention: whole pages + own tokens
+    (16, 28, 4, 77, 777, 77, True, 3, 2),       # the encoder tail: GQA 7, causal own keys
+    (128, 3, 3, 130, 300, 45, False, 1, 0),     # one page per tile
+    (256, 2, 1, 257, 700, 0, False, 2, 0),      # pages larger than a tile, GQA 2
+    (8, 2, 2, 40, 100, 37, True, 1, 0),         # 16 small pages per tile, more queries than own keys
+    (32, 2, 2, 1, 33, 1, True, 1, 0),           # one query
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(map(str, c)))
+def test_paged_attention_matches_fp32(case):
+    page, hq, hkv, n_q, n_prefix, n_local, causal, layers, layer = case
+    n_pages = -(-n_prefix // page) + 3
+    pool = _pool(layers, hkv, page, n_pages, seed=page)
+    slots, vals = _prefix(pool, n_prefix, seed=n_prefix)
+    g = torch.Generator(device=DEV).manual_seed(7)
+    q = torch.randn(n_q, hq, D, generator=g, device=DEV).bfloat16()
+    k_own = torch.randn(n_local, hkv, D, generator=g, device=DEV).bfloat16() if n_local else None
+    v_own = torch.randn(n_local, hkv, D, generator=g, device=DEV).bfloat16() if n_local else None
+    scale = 1 / math.sqrt(D)
+    out, lse = paged_attention(q, PagedPrefix(pool, slots), layer, k_own, v_own, causal=causal, scale=scale,
+                               return_lse=True)
+    torch.cuda.synchronize()
+    assert pool.device_errors() == 0
+    k = vals[layer, 0] if n_local == 0 else torch.cat([vals[layer, 0], k_own])
+    v = vals[layer, 1] if n_local == 0 else torch.cat([vals[layer, 1], v_own])
+    ref_out, ref_lse = _reference(q, k, v, scale, causal, n_local)
+    _check(out, lse, ref_out, ref_lse)
+
+
+def test_own_keys_only_causal():
+    """No prefix (a first turn): causal attention over the step's own keys only."""
+    g = torch.Generator(device=DEV).manual_seed(3)
+    n, h = 333, 2
+    q, k, v = (torch.randn(n, h, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+    out, lse = paged_attention(q, None, 0, k, v, causal=True, return_lse=True)
+    ref_out, ref_lse = _reference(q, k, v, 1 / math.sqrt(D), True, n)
+    _check(out, lse, ref_out, ref_lse)
+
+
+def test_growing_maximum_rescales_the_output():
+    """Scores whose row maximum keeps growing from tile to tile by more than the lazy-rescale threshold, with a
+    sharp softmax: the O rescale path has to be exact."""
+    page, h, n_prefix = 64, 2, 1024
+    pool = _pool(1, h, page, n_prefix // page + 2, seed=1)
+    slots, vals = _prefix(pool, n_prefix, seed=2)
+    ramp = torch.linspace(0.2, 3.0, n_prefix, device=DEV)[:, None, None]
+    vals[0, 0] = (vals[0, 0].float() * ramp).bfloat16()  # later keys: larger scores
+    pool.kv[:, :, slots] = vals
+    g = torch.Generator(device=DEV).manual_seed(4)
+    q = (torch.randn(256, h, D, generator=g, device=DEV) * 3).bfloat16()
+    out, lse = paged_attention(q, PagedPrefix(pool, slots), 0, return_lse=True)
+    ref_out, ref_lse = _reference(q, vals[0, 0], vals[0, 1], 1 / math.sqrt(D), False, 0)
+    _check(out, lse, ref_out, ref_lse)
+
+
+def test_page_outside_the_pool_reads_zeros_and_is_reported():
+    page, h, n_prefix = 64, 2, 256
+    pool = _pool(1, h, page, 6, seed=5)
+    slots, vals = _prefix(pool, n_prefix, seed=6)
+    prefix = PagedPrefix(pool, slots)
+    prefix.block_table[2] = pool.rows // page + 5  # the third page points past the pool
+    g = torch.Generator(device=DEV).manual_seed(8)
+    q = torch.randn(128, h, D, generator=g, device=DEV).bfloat16()
+    out = paged_attention(q, prefix, 0)
+    torch.cuda.synchronize()
+    assert pool.device_errors() & 1
+    k, v = vals[0, 0].clone(), vals[0, 1].clone()
+    k[2 * page: 3 * page] = 0
+    v[2 * page: 3 * page] = 0
+    ref_out, _ = _reference(q, k, v, 1 / math.sqrt(D), False, 0)
+    _check(out, None, ref_out, None)
+
+
+def test_one_k_edit_layer_joint_attention():
+    """One DiT layer of the 1K edit: 4096 latent queries over the 4608-token prefix (page 64, scattered pages)
+    and their own 4096 keys, 24 heads; checked on every head."""
+    page, h, n_prefix, n = 64, 24, 4608, 4096
+    pool = _pool(1, h, page, n_prefix // page + 4, seed=9)
+    slots, vals = _prefix(pool, n_prefix, seed=10)
+    g = torch.Generator(device=DEV).manual_seed(11)
+    q, k_own, v_own = (torch.randn(n, h, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+    out, lse = paged_attention(q, PagedPrefix(pool, slots), 0, k_own, v_own, return_lse=True)
+    k = torch.cat([vals[0, 0], k_own])
+    v = torch.cat([vals[0, 1], v_own])
+    for h0 in range(0, h, 6):  # the fp32 reference in slices of heads
+        ref_out, ref_lse = _reference(q[:, h0:h0 + 6], k[:, h0:h0 + 6], v[:, h0:h0 + 6], 1 / math.sqrt(D), False, 0)
+        _check(out[:, h0:h0 + 6], lse[h0:h0 + 6], ref_out, ref_lse)
+
+
+def test_strided_views_in_and_out():
+    """q, own K/V and out as head slices of wider token rows (as projections produce them)."""
+    page, h, n_prefix, n = 32, 2, 200, 150
+    pool = _pool(1, h, page, n_prefix // page + 3, seed=12)
+    slots, vals = _prefix(pool, n_prefix, seed=13)
+    g = torch.Generator(device=DEV).manual_seed(14)
+    qkv = torch.randn(n, 3 * h, D, generator=g, device=DEV).bfloat16()
+    q, k_own, v_own = qkv[:, :h], qkv[:, h:2 * h], qkv[:, 2 * h:]
+    wide = torch.zeros(n, 4 * h, D, dtype=torch.bfloat16, device=DEV)
+    out = paged_attention(q, PagedPrefix(pool, slots), 0, k_own, v_own, out=wide[:, h:2 * h])
+    assert out.data_ptr() == wide[:, h:2 * h].data_ptr()
+    ref_out, _ = _reference(q, torch.cat([vals[0, 0], k_own]), torch.cat([vals[0, 1], v_own]), 1 / math.sqrt(D),
+                            False, 0)
+    _check(out, None, ref_out, None)
+    assert bool((wide[:, :h] == 0).all()) and bool((wide[:, 2 * h:] == 0).all())

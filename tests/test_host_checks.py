@@ -148,3 +148,41 @@ def test_nvfp4_numerics_setter_checks_its_fields():
     assert NUMERICS == {"ieee": 0, "triton": 21}
     set_numerics("ieee")
     set_numerics("triton")  # the default, restored
+
+
+def test_paged_attention_checks_arguments_before_any_cuda_call():
+    from qwenedit_b200 import _lib
+    from qwenedit_b200.attention import paged_attention
+
+    q = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_attention(q, None, 0, q, q)
+
+    def call(**kw):
+        args = dict(q=16, qt=512, qh=256, n_q=4, hq=2, kp=16, vp=16, rows=128, hkv=2, bt=16, page=64, n_pre=10,
+                    kl=None, vl=None, lt=0, lh=0, n_loc=0, causal=0, scale=0.088, out=16, ot=512, oh=256, lse=None,
+                    err=None, stream=None)
+        args.update(kw)
+        _lib.call("qe_paged_attention", *args.values())
+
+    with pytest.raises(ValueError, match="multiple of heads_kv"):
+        call(hq=3)
+    with pytest.raises(ValueError, match="page_size"):
+        call(page=12)
+    with pytest.raises(ValueError, match="page_size"):
+        call(page=4)
+    with pytest.raises(ValueError, match="pool_rows"):
+        call(rows=100)
+    with pytest.raises(ValueError, match="null q"):
+        call(q=None)
+    with pytest.raises(ValueError, match="no keys"):
+        call(n_pre=0)
+    with pytest.raises(ValueError, match="16-byte"):
+        call(qt=200)
+    with pytest.raises(ValueError, match="scale"):
+        call(scale=float("nan"))
+    with pytest.raises(ValueError, match="null pool"):
+        call(bt=None)
+    with pytest.raises(ValueError, match="local"):
+        call(n_loc=5)
+    call(n_q=0)  # nothing to do: returns before touching the GPU
