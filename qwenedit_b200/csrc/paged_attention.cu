@@ -196,6 +196,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -209,7 +217,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kpool,
                            const __grid_constant__ CUtensorMap tm_vpool, const __grid_constant__ CUtensorMap tm_ktail,
                            const __grid_constant__ CUtensorMap tm_vtail, const __grid_constant__ CUtensorMap tm_klocal,
@@ -411,19 +419,14 @@ __global__ void __maxnreg__(200)
         limit = p.n_local - l0;
         if (p.causal) limit = min(limit, qi + causal_shift - l0 + 1);
       }
-      float s[kTile];
+      // pass 1: the row's max over the visible keys (S stays in tensor memory; 32 columns at a time)
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float chunk[32];
         tmem_ld32(s_col + 32 * c, chunk);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 * c + i] = chunk[i];
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kTile; ++c) {
-        s[c] = c < limit ? s[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, 32 * c + i < limit ? chunk[i] * p.scale_log2 : -INFINITY);
       }
       // A row moves its reference max only when its max grew by more than 2^8 (also when m_use is still -inf and
       // a key is visible); its O (earlier tiles' sums at the old max) is scaled down to match. The tensor-memory
@@ -445,17 +448,23 @@ __global__ void __maxnreg__(200)
         l *= f;
         if (grow) m_use = mx;
       }
+      // pass 2: p = 2^(s - base) as bf16 pairs over the consumed S columns: chunk c's 32 scores (columns 32c ..)
+      // become P columns 16c .. 16c + 15, all of which pass 2 has already read
       const float base = m_use == -INFINITY ? 0.0f : m_use;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t w[32];
+      for (int c = 0; c < 4; ++c) {
+        float chunk[32];
+        uint32_t w[16];
+        tmem_ld32(s_col + 32 * c, chunk);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = ex2(s[64 * h + 2 * i] - base), b = ex2(s[64 * h + 2 * i + 1] - base);
+        for (int i = 0; i < 16; ++i) {
+          const int k = 32 * c + 2 * i;
+          const float a = k < limit ? ex2(chunk[2 * i] * p.scale_log2 - base) : 0.0f;
+          const float b = k + 1 < limit ? ex2(chunk[2 * i + 1] * p.scale_log2 - base) : 0.0f;
           l += a + b;
           w[i] = pack_bf16(a, b);
         }
-        tmem_st32(s_col + 32 * h, w);
+        tmem_st16(s_col + 16 * c, w);
       }
       tmem_wait_st();
       tc_fence_before();
