@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
     ap.add_argument("--workload", choices=["edit_1k", "serving", "headshard"], default="edit_1k",
                     help="edit_1k: the 1K-edit turn (default, the headline); serving: 64 mixed 1K/2K sessions")
-    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu", "short_rows"], default=None,
+    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu", "short_rows", "attention"], default=None,
                     help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
     return ap.parse_args()
 
@@ -390,6 +390,7 @@ def extras(pool, sess, device):
     m.release()
     del big
     torch.cuda.empty_cache()
+    out["paged_attention_1k"] = attention_extras(pool, device)
     out.update(nvfp4_extras(device, peak))
     out["nvfp4_cpu_baseline"] = nvfp4_cpu()
     out["mask_blend_1k"] = latent_extras(device)
@@ -527,6 +528,84 @@ def latent_extras(device):
     return {"device_us_per_call": round(device_us, 2), "host_us_per_call": round(host_us, 1),
             "launches_per_call": 1, "bytes_per_call": nbytes,
             "GB/s": round(nbytes / device_us / 1e3, 1)}
+
+
+def attention_extras(pool, device):
+    """One DiT step's joint attention at the 1K edit (60 layers; 4096 latent queries over the 4608-token pooled
+    prefix, page 64 through a shuffled block table, plus their own 4096 keys; 24 heads x 128): the paged kernel
+    (qe_paged_attention, one launch per layer, prefix read from the pool pages) against the path it replaces, one
+    gather of the prefix for all layers followed per layer by a concatenation with the own K/V and torch's SDPA
+    (cuDNN backend, the fastest library attention on this GPU). FLOPs per layer 4 n_q (n_prefix + n_own) D H."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from qwenedit_b200.attention import PagedPrefix, paged_attention
+
+    pool.clear()
+    pool.index.shuffle_free(11)
+    vids = np.arange(1, PREFIX + 1, dtype=np.int64) + (1 << 41)
+    slots = pool.alloc(PREFIX)
+    pool.insert(vids, slots, owned_from=0)
+    m = pool.match(vids)
+    prefix = PagedPrefix(pool, m.indices)
+    n = IMAGE
+    g = torch.Generator(device=device).manual_seed(0)
+    q, k_own, v_own = (torch.randn(n, H, D, generator=g, device=device).bfloat16() for _ in range(3))
+    out = torch.empty(n, H, D, dtype=torch.bfloat16, device=device)
+    flops_layer = 4.0 * n * (PREFIX + n) * D * H
+
+    def ours():
+        for layer in range(L):
+            paged_attention(q, prefix, layer, k_own, v_own, out=out)
+
+    gathered = torch.empty(L, 2, PREFIX, H, D, dtype=torch.bfloat16, device=device)
+    qh = q.transpose(0, 1)[None]
+
+    def gather_then_sdpa():
+        pool.gather_into(m.indices, gathered)
+        for layer in range(L):
+            k = torch.cat([gathered[layer, 0], k_own]).transpose(0, 1)[None]
+            v = torch.cat([gathered[layer, 1], v_own]).transpose(0, 1)[None]
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                F.scaled_dot_product_attention(qh, k, v)
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    ms = timed(ours)
+    try:
+        ms_ref = timed(gather_then_sdpa)
+    except Exception:  # noqa: BLE001  (no cuDNN attention in this torch build)
+        ms_ref = None
+    if pool.device_errors():
+        raise RuntimeError("the paged attention kernel reported an error")
+    peaks = {}
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+    tf = flops_layer * L / ms / 1e9
+    res = {"layers": L, "queries": n, "prefix_tokens": PREFIX, "own_tokens": n, "heads": H,
+           "ms_per_step": round(ms, 3), "ms_per_layer": round(ms / L, 4), "TFLOP/s": round(tf, 1),
+           "gather_then_cudnn_sdpa_ms_per_step": None if ms_ref is None else round(ms_ref, 3),
+           "speedup_vs_gather_then_cudnn_sdpa": None if ms_ref is None else round(ms_ref / ms, 3),
+           "timing": "CUDA events around one step's 60 launches (inputs resident, 2.3 GB of prefix K/V per step > L2)"}
+    if peaks.get("bf16_tflops_sustained"):
+        res["frac_of_measured_bf16_sustained"] = round(tf / peaks["bf16_tflops_sustained"], 4)
+        res["frac_of_measured_bf16_burst"] = round(tf / peaks["bf16_tflops"], 4)
+    m.release()
+    del gathered
+    torch.cuda.empty_cache()
+    return res
 
 
 def _time_kernel(fn, flush, iters=20):
@@ -1025,6 +1104,16 @@ def profile_case(kind: str) -> None:
         slots = pool.alloc(n)
         buf = torch.empty(L, 2, n, hl, D, dtype=torch.bfloat16, device=device)
         fn = lambda: pool.gather_into(slots, buf)  # noqa: E731
+    elif kind == "attention":  # one layer of the 1K edit's joint attention (4096 queries, 4608 + 4096 keys, 24 heads)
+        from qwenedit_b200.attention import PagedPrefix, paged_attention
+
+        pool = PagedKVPool("dit", 1, H, D, (PREFIX + 2 * PAGE) * 2 * ROW, torch.bfloat16, device, page_size=PAGE)
+        pool.index.shuffle_free(5)
+        pool.kv.normal_()
+        prefix = PagedPrefix(pool, pool.alloc(PREFIX))
+        q, k_own, v_own = (torch.randn(IMAGE, H, D, device=device).bfloat16() for _ in range(3))
+        out = torch.empty_like(q)
+        fn = lambda: paged_attention(q, prefix, 0, k_own, v_own, out=out)  # noqa: E731
     elif kind == "norm":
         T, K = 32768, 3072
         x = torch.randn(1, T, K, dtype=torch.bfloat16, device=device)

@@ -206,6 +206,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -419,15 +424,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         limit = p.n_local - l0;
         if (p.causal) limit = min(limit, qi + causal_shift - l0 + 1);
       }
-      // pass 1: the row's max over the visible keys (S stays in tensor memory; 32 columns at a time)
-      float mx = -INFINITY;
+      // Tiles whose 128 keys are all visible to every row of the warp skip the per-key masks (warp-uniform).
+      const bool masked = __any_sync(0xffffffffu, limit < kTile);
+      // pass 1: the row's max of the raw scores over the visible keys (S stays in tensor memory, read 32
+      // columns at a time; four independent three-input max chains), scaled once afterwards (scale > 0)
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float chunk[32];
         tmem_ld32(s_col + 32 * c, chunk);
+        if (masked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, 32 * c + i < limit ? chunk[i] * p.scale_log2 : -INFINITY);
+          for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          m4[0] = max3(m4[0], chunk[i], chunk[i + 1]);
+          m4[1] = max3(m4[1], chunk[i + 2], chunk[i + 3]);
+          m4[2] = max3(m4[2], chunk[i + 4], chunk[i + 5]);
+          m4[3] = max3(m4[3], chunk[i + 6], chunk[i + 7]);
+        }
       }
+      const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
       // A row moves its reference max only when its max grew by more than 2^8 (also when m_use is still -inf and
       // a key is visible); its O (earlier tiles' sums at the old max) is scaled down to match. The tensor-memory
       // accesses are warp-collective, so a warp rescales together: rows that keep their max scale by 1.
@@ -448,24 +466,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= f;
         if (grow) m_use = mx;
       }
-      // pass 2: p = 2^(s - base) as bf16 pairs over the consumed S columns: chunk c's 32 scores (columns 32c ..)
-      // become P columns 16c .. 16c + 15, all of which pass 2 has already read
-      const float base = m_use == -INFINITY ? 0.0f : m_use;
+      // pass 2: p = 2^(s scale_log2 - base) (one FFMA and one ex2 per key) as bf16 pairs written over the S
+      // columns already read: chunk c's 32 scores (columns 32c ..) become P columns 16c .. 16c + 15. The row sum
+      // runs in eight independent partial sums.
+      const float nbase = m_use == -INFINITY ? 0.0f : -m_use;
+      float l8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float chunk[32];
         uint32_t w[16];
         tmem_ld32(s_col + 32 * c, chunk);
 #pragma unroll
+        for (int i = 0; i < 32; ++i) chunk[i] = ex2(fmaf(chunk[i], p.scale_log2, nbase));
+        if (masked) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
+        }
+#pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int k = 32 * c + 2 * i;
-          const float a = k < limit ? ex2(chunk[2 * i] * p.scale_log2 - base) : 0.0f;
-          const float b = k + 1 < limit ? ex2(chunk[2 * i + 1] * p.scale_log2 - base) : 0.0f;
-          l += a + b;
-          w[i] = pack_bf16(a, b);
+          l8[i & 7] += chunk[2 * i] + chunk[2 * i + 1];
+          w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
         }
         tmem_st16(s_col + 16 * c, w);
       }
+      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kPReady + t));
