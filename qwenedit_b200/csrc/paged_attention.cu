@@ -206,6 +206,28 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// packed pairs of fp32 (Blackwell f32x2 arithmetic: one instruction for two lanes' worth of work)
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 up2(f32x2 r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -470,26 +492,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       // columns already read: chunk c's 32 scores (columns 32c ..) become P columns 16c .. 16c + 15. The row sum
       // runs in eight independent partial sums.
       const float nbase = m_use == -INFINITY ? 0.0f : -m_use;
-      float l8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      const f32x2 scale2 = pk2(p.scale_log2, p.scale_log2), nbase2 = pk2(nbase, nbase);
+      f32x2 l4[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float chunk[32];
         uint32_t w[16];
         tmem_ld32(s_col + 32 * c, chunk);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) chunk[i] = ex2(fmaf(chunk[i], p.scale_log2, nbase));
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = up2(fma2(pk2(chunk[2 * i], chunk[2 * i + 1]), scale2, nbase2));
+          chunk[2 * i] = ex2(x.x);
+          chunk[2 * i + 1] = ex2(x.y);
+        }
         if (masked) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          l8[i & 7] += chunk[2 * i] + chunk[2 * i + 1];
+          l4[i & 3] = add2(l4[i & 3], pk2(chunk[2 * i], chunk[2 * i + 1]));
           w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
         }
         tmem_st16(s_col + 16 * c, w);
       }
-      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      {
+        const float2 a = up2(add2(add2(l4[0], l4[1]), add2(l4[2], l4[3])));
+        l += a.x + a.y;
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kPReady + t));
