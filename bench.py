@@ -66,7 +66,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the 2K and NVFP4 side measurements")
     ap.add_argument("--workload", choices=["edit_1k", "serving", "headshard"], default="edit_1k",
                     help="edit_1k: the 1K-edit turn (default, the headline); serving: 64 mixed 1K/2K sessions")
-    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu", "short_rows", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gather", "append", "norm", "silu", "short_rows", "attention", "gather_heads",
+                                                   "mask_blend", "norm_amax", "silu_amax"], default=None,
                     help="small case for ncu: 3 warm-up + 3 launches of one kernel (a few GB on the device)")
     return ap.parse_args()
 
@@ -1114,6 +1115,32 @@ def profile_case(kind: str) -> None:
         q, k_own, v_own = (torch.randn(IMAGE, H, D, device=device).bfloat16() for _ in range(3))
         out = torch.empty_like(q)
         fn = lambda: paged_attention(q, prefix, 0, k_own, v_own, out=out)  # noqa: E731
+    elif kind == "gather_heads":  # the encoder's partial hit: 28 layers x 4 heads, 4096 prefix tokens head-major
+        pool = PagedKVPool("encoder", 28, 4, D, 8192 * 28 * 2 * 4 * D * 2, torch.bfloat16, device)
+        pool.index.shuffle_free(5)
+        pool.kv.normal_()
+        slots = pool.alloc(4096)
+        fn = lambda: pool.gather_heads(slots, 4096 + 256)  # noqa: E731
+    elif kind == "mask_blend":  # per-step latent blend on 16 x 16384 x 64 bf16 latents (inputs > L2 in total)
+        from qwenedit_b200.latents import mask_blend
+
+        lat = torch.randn(16, 16384, 64, device=device).bfloat16()
+        x0, eps = torch.randn_like(lat), torch.randn_like(lat)
+        msk = torch.rand(16, 16384, 1, device=device)
+        sigma = torch.tensor(0.5, device=device)
+        fn = lambda: mask_blend(lat, x0, eps, msk, sigma)  # noqa: E731
+    elif kind in ("norm_amax", "silu_amax"):
+        from qwenedit_b200.fp4 import norm_scale_amax, silu_mul_amax
+
+        if kind == "norm_amax":
+            x = torch.randn(1, 32768, 3072, dtype=torch.bfloat16, device=device)
+            norm = SimpleNamespace(weight=torch.ones(3072, dtype=torch.bfloat16, device=device), eps=1e-6)
+            sc = (0.1 * torch.randn(1, 3072, device=device)).bfloat16()
+            fn = lambda: norm_scale_amax(x, norm, sc, None, None, shift=sc)  # noqa: E731
+        else:
+            g = torch.randn(4096, 12288, dtype=torch.bfloat16, device=device)
+            v = torch.randn(4096, 12288, dtype=torch.bfloat16, device=device)
+            fn = lambda: silu_mul_amax(g, v)  # noqa: E731
     elif kind == "norm":
         T, K = 32768, 3072
         x = torch.randn(1, T, K, dtype=torch.bfloat16, device=device)
