@@ -131,16 +131,17 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback (6.65 TB/s pool figure)"
 
 
-def committed_traffic(kernel: str) -> float | None:
-    """DRAM bytes per launch of `kernel` from the committed ncu summary (profiles/traffic.txt), if present."""
+def committed_traffic(kernel: str) -> dict | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (profiles/traffic.txt): read and write
+    separately (the write count is a lower bound: lines still dirty in L2 when the kernel ends are not counted)."""
     path = ROOT / "profiles" / "traffic.txt"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
         parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel:
+        if len(parts) >= 3 and parts[0] == kernel:
             try:
-                return float(parts[1])
+                return {"read": float(parts[1]), "write": float(parts[2])}
             except ValueError:
                 return None
     return None
@@ -1215,7 +1216,12 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
             "dit_step_ms_1k": round(r["avg_gather_ms"], 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": "paged_gather (block table)",
+                         "frac": round(achieved / peak, 4),
+                         "traffic": None if traffic is None else traffic["read"] + traffic["write"],
+                         "traffic_read": None if traffic is None else traffic["read"],
+                         "traffic_write_lower_bound": None if traffic is None else traffic["write"],
+                         "traffic_source": "ncu, full 60-layer launch (profiles/small_kernels.md)",
+                         "kernel": "paged_gather (block table)",
                          "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": GATHER_BYTES},
             "frac_of_measured_hbm": round(value / world / peak, 4),
