@@ -101,6 +101,114 @@ __global__ void __launch_bounds__(256) mask_blend_kernel(BlendParams p) {
   }
 }
 
+// The same blend, 8 channels of one latent cell per thread: the cell's (b, n) index is found once per 8 values
+// with 32-bit arithmetic (B * N * C / 8 < 2^31, C a multiple of 8), the three latent tensors move as 16-byte
+// (32-byte for fp32) vectors and a per-cell mask (mask_channels == 1) is loaded once. Same op order and roundings
+// per value as mask_blend_kernel.
+template <int kT>
+struct Vec8;
+template <>
+struct Vec8<kBF16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16 *p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = u;
+  }
+};
+template <>
+struct Vec8<kF16> {
+  static __device__ __forceinline__ void load(const __half *p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(__half *p, const float (&v)[8]) {
+    uint4 u;
+    __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = u;
+  }
+};
+template <>
+struct Vec8<kF32> {
+  static __device__ __forceinline__ void load(const float *p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(float *p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+template <int kT>
+__global__ void __launch_bounds__(256) mask_blend_vec_kernel(BlendParams p) {
+  using E = Elem<kT>;
+  using T = typename E::T;
+  float s, oms;
+  if (p.sigma_dtype == kScalarPair) {
+    s = static_cast<const float *>(p.sigma)[0];
+    oms = static_cast<const float *>(p.sigma)[1];
+  } else {
+    s = E::rnd(load_any(p.sigma, p.sigma_dtype, 0));
+    oms = E::rnd(__fsub_rn(1.0f, s));
+  }
+  const uint32_t vpc = uint32_t(p.C >> 3), N = uint32_t(p.N);
+  const uint32_t total = uint32_t(p.B) * N * vpc;
+  const T *lat = static_cast<const T *>(p.lat);
+  const T *x0 = static_cast<const T *>(p.x0);
+  const T *eps = static_cast<const T *>(p.eps);
+  T *out = static_cast<T *>(p.out);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t cell = i / vpc, ch = (i - cell * vpc) * 8;
+    const uint32_t b = cell / N, n = cell - b * N;
+    const int64_t nc = int64_t(n) * p.C + ch;
+    float xl[8], xx[8], xe[8], m8[8];
+    Vec8<kT>::load(lat + int64_t(i) * 8, xl);
+    Vec8<kT>::load(x0 + int64_t(b) * p.x0_bstride + nc, xx);
+    Vec8<kT>::load(eps + int64_t(b) * p.eps_bstride + nc, xe);
+    const int64_t mrow = int64_t(b) * p.mask_bstride + int64_t(n) * p.mask_channels;
+    if (p.mask_channels == 1) {
+      const float m = E::rnd(load_any(p.mask, p.mask_dtype, mrow));  // editable.to(dtype)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = m;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = E::rnd(load_any(p.mask, p.mask_dtype, mrow + ch + k));
+    }
+    float o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float a = E::rnd(__fmul_rn(oms, xx[k]));
+      const float e = E::rnd(__fmul_rn(s, xe[k]));
+      const float keep = E::rnd(__fadd_rn(a, e));
+      const float ml = E::rnd(__fmul_rn(m8[k], xl[k]));
+      const float omm = E::rnd(__fsub_rn(1.0f, m8[k]));
+      const float mk = E::rnd(__fmul_rn(omm, keep));
+      o[k] = __fadd_rn(ml, mk);
+    }
+    Vec8<kT>::store(out + int64_t(i) * 8, o);
+  }
+}
+
 // out[h, w, C] = base everywhere, crop[(y - y0), (x - x0), C] inside the box; 16-byte vectors when C allows
 template <typename V>
 __global__ void __launch_bounds__(256) compose_kernel(const V *base, const V *crop, V *out, int64_t h, int64_t w,
@@ -157,6 +265,20 @@ int qe_mask_blend(const void *latents, const void *x0, const void *eps, const vo
   qe::BlendParams p{latents, x0, eps, mask, sigma, out, B, N, C, x0_bstride, eps_bstride, mask_bstride,
                     mask_channels, mask_dtype, sigma_dtype};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t esz = dtype == qe::kF32 ? 4 : 2;
+  const bool vec = C % 8 == 0 && total / 8 < (int64_t(1) << 31) && N < (int64_t(1) << 31) &&
+                   x0_bstride % 8 == 0 && eps_bstride % 8 == 0 && qe::aligned16(latents) && qe::aligned16(x0) &&
+                   qe::aligned16(eps) && qe::aligned16(out) && (esz * 8) % 16 == 0;
+  if (vec) {
+    const int grid = qe::grid_for(total / 8);
+    switch (dtype) {
+      case qe::kBF16: qe::mask_blend_vec_kernel<qe::kBF16><<<grid, 256, 0, st>>>(p); break;
+      case qe::kF16: qe::mask_blend_vec_kernel<qe::kF16><<<grid, 256, 0, st>>>(p); break;
+      default: qe::mask_blend_vec_kernel<qe::kF32><<<grid, 256, 0, st>>>(p); break;
+    }
+    int s = qe::cuda_status(cudaGetLastError(), "qe_mask_blend launch");
+    return s ? s : qe::ok();
+  }
   const int grid = qe::grid_for(total);
   switch (dtype) {
     case qe::kBF16: qe::mask_blend_kernel<qe::kBF16><<<grid, 256, 0, st>>>(p); break;

@@ -43,6 +43,20 @@ def test_mask_blend_latent_dtype_mask_per_channel():
     assert torch.equal(latents.mask_blend(lat, x0, eps, m, s), latents_ref.blend(lat, x0, eps, m, s))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_mask_blend_element_path(dtype):
+    """Shapes the 8-channel vector kernel does not take (C not a multiple of 8; latents 2 elements off a 16-byte
+    boundary) run the per-element kernel, with the same result as eager."""
+    lat, x0, eps, m = _case(2, 999, 12, dtype, seed=7)
+    s = torch.tensor(0.41, dtype=torch.float32, device=DEV)
+    assert torch.equal(latents.mask_blend(lat, x0, eps, m, s), latents_ref.blend(lat, x0, eps, m, s))
+    lat, x0, eps, m = _case(1, 512, 64, dtype, seed=8)
+    buf = torch.empty(lat.numel() + 1, dtype=dtype, device=DEV)
+    shifted = buf[1:].view(lat.shape)
+    shifted.copy_(lat)
+    assert torch.equal(latents.mask_blend(shifted, x0, eps, m, s), latents_ref.blend(lat, x0, eps, m, s))
+
+
 @pytest.mark.parametrize("box", [(0, 0, 64, 64), (3, 5, 17, 40), (60, 0, 64, 1), (0, 63, 64, 64)])
 @pytest.mark.parametrize("C,dtype", [(64, torch.bfloat16), (16, torch.float32), (3, torch.float16)])
 def test_compose_and_crop_match_eager(box, C, dtype):
