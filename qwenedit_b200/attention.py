@@ -119,3 +119,60 @@ def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0,
                   None if lse is None else lse.data_ptr(), None if err is None else err.data_ptr(),
                   _lib.stream_of(device))
     return (out, lse) if return_lse else out
+
+
+def encoder_tail_attention(q: torch.Tensor, k_tail: torch.Tensor, v_tail: torch.Tensor, pool, indices: torch.Tensor,
+                           layer: int, scale: float, heads_buf: torch.Tensor | None = None) -> torch.Tensor:
+    """One text-encoder layer's attention on a partial prefix hit (cache/encoder.py:173-190): the n tail queries
+    attend over [the m cached prefix tokens; the n tail tokens], tail position i seeing the prefix and tail [0, i]
+    (the reference's ``ones(n, m + n).tril(diagonal=m)`` mask), grouped-query heads (enable_gqa).
+
+    q [n, Hq, 128], k_tail / v_tail [n, Hkv, 128] bf16 (token-major: the reference's ``k[0].transpose(0, 1)``).
+    A page-mode pool (page size 8 to 128, or a multiple of 128) is read through its block table by the attention
+    kernel itself. A token-granular pool (the reference's page size 1) is first gathered head-major with room for
+    the tail (``pool.gather_heads``; pass the same `heads_buf` to every layer so it is gathered once), the tail
+    K/V written after the prefix, and the kernel attends over that buffer. Returns [n, Hq, 128] bf16."""
+    n = q.shape[0]
+    m = int(indices.numel())
+    if pool.page_size >= 8 and (128 % pool.page_size == 0 or pool.page_size % 128 == 0):
+        return paged_attention(q, PagedPrefix(pool, indices) if m else None, layer, k_tail, v_tail, causal=True,
+                               scale=scale)
+    if heads_buf is None:
+        heads_buf = pool.gather_heads(indices, m + n)
+    if heads_buf.shape[3] != m + n:
+        raise ValueError(f"heads_buf holds {heads_buf.shape[3]} positions, expected {m + n}")
+    kh, vh = heads_buf[layer, 0], heads_buf[layer, 1]  # [Hkv, m + n, D]
+    kh[:, m:].copy_(k_tail.transpose(0, 1))
+    vh[:, m:].copy_(v_tail.transpose(0, 1))
+    return paged_attention(q, None, layer, kh.transpose(0, 1), vh.transpose(0, 1), causal=True, scale=scale)
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, prefix: PagedPrefix | None, layer: int,
+                      segments, start: int, scale: float | None = None) -> torch.Tensor:
+    """The attention of the DiT's prefix prefill from position `start` (cache/prefill.py:32-72), one layer: the
+    prefix positions [start, total) attend per segment (s, e, is_image) over keys [0, e), causally inside text
+    segments (a text query at position p sees keys <= p), fully inside image segments. Keys [0, start) are the
+    pooled prefix (read through the block table); keys [start, e) are this call's own k / v.
+
+    q, k, v [total - start, H, 128] bf16 for positions start .. total - 1; `segments` as the reference's layout
+    (start and end positions over the whole prefix). Returns [total - start, H, 128]; one kernel launch per
+    segment that starts past `start`."""
+    n = q.shape[0]
+    for s0, e, is_image in segments:  # as the reference checks before any layer runs
+        if is_image and s0 < start < e:
+            raise ValueError("cached prefix ends inside an image block")
+    if start and (prefix is None or prefix.length != start):
+        raise ValueError(f"the pooled prefix must hold the {start} positions before `start`")
+    out = torch.empty_like(q)
+    for s0, e, is_image in segments:
+        if e <= start:
+            continue
+        s = max(s0, start)
+        if is_image and s0 < start:
+            raise ValueError("cached prefix ends inside an image block")
+        lo, hi = s - start, e - start
+        if hi > n:
+            raise ValueError(f"segment ends at {e}, past the {start + n} positions given")
+        paged_attention(q[lo:hi], prefix if start else None, layer, k[:hi], v[:hi], causal=not is_image,
+                        scale=scale, out=out[lo:hi])
+    return out

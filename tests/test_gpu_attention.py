@@ -182,3 +182,80 @@ def test_strided_views_in_and_out():
                             False, 0)
     _check(out, None, ref_out, None)
     assert bool((wide[:, :h] == 0).all()) and bool((wide[:, 2 * h:] == 0).all())
+
+
+# ---- the tail computations either side of the pool (f2): encoder partial hit, DiT prefix prefill ----------------
+def _sdpa_ref(q, k, v, mask, scale):
+    """fp32 attention with a boolean visibility mask [n_q, n_k], GQA by head repetition (the reference's
+    F.scaled_dot_product_attention(..., attn_mask=mask, enable_gqa=True))."""
+    group = q.shape[1] // k.shape[1]
+    qf = q.float().transpose(0, 1)
+    kf = k.float().transpose(0, 1).repeat_interleave(group, 0)
+    vf = v.float().transpose(0, 1).repeat_interleave(group, 0)
+    s = (qf @ kf.transpose(1, 2) * scale).masked_fill(~mask, float("-inf"))
+    return (torch.softmax(s, dim=-1) @ vf).transpose(0, 1)
+
+
+@pytest.mark.parametrize("page", [16, 1])
+def test_encoder_tail_attention_matches_the_reference_mask(page):
+    """cache/encoder.py:173-190: tail queries over [cached prefix; tail] with ones(n, m + n).tril(diagonal=m),
+    grouped-query heads 28 / 4. Page 16: the kernel reads the pool pages; page 1 (token-granular, the reference's
+    pool): the head-major gather feeds the kernel, the tail written after the prefix."""
+    from qwenedit_b200.attention import encoder_tail_attention
+
+    layers, hq, hkv, m, n = 3, 28, 4, 777, 77
+    pool = _pool(layers, hkv, page, -(-m // page) + 4, seed=21)
+    slots, vals = _prefix(pool, m, seed=22)
+    g = torch.Generator(device=DEV).manual_seed(23)
+    scale = 128 ** -0.5
+    heads_buf = None if page > 1 else pool.gather_heads(slots, m + n)
+    for layer in range(layers):
+        q = torch.randn(n, hq, D, generator=g, device=DEV).bfloat16()
+        k_t, v_t = (torch.randn(n, hkv, D, generator=g, device=DEV).bfloat16() for _ in range(2))
+        out = encoder_tail_attention(q, k_t, v_t, pool, slots, layer, scale, heads_buf=heads_buf)
+        mask = torch.ones(n, m + n, dtype=torch.bool, device=DEV).tril(diagonal=m)
+        ref = _sdpa_ref(q, torch.cat([vals[layer, 0], k_t]), torch.cat([vals[layer, 1], v_t]), mask, scale)
+        _check(out, None, ref, None)
+        if heads_buf is not None:
+            assert torch.equal(heads_buf[layer, 0, :, m:], k_t.transpose(0, 1))
+
+
+@pytest.mark.parametrize("start", [0, 100, 700])
+def test_prefill_attention_matches_the_segment_loop(start):
+    """cache/prefill.py:52-66: each segment (s, e, is_image) of positions [start, total) attends over keys [0, e),
+    causally inside text segments; keys before `start` come from the pool."""
+    from qwenedit_b200.attention import prefill_attention
+
+    h, total = 4, 900
+    segments = [(0, 100, False), (100, 612, True), (612, 900, False)]
+    pool = _pool(2, h, 64, 16, seed=31)
+    layer = 1
+    if start:
+        slots, vals = _prefix(pool, start, seed=32)
+        pre_k, pre_v = vals[layer, 0], vals[layer, 1]
+        prefix = PagedPrefix(pool, slots)
+    else:
+        pre_k = pre_v = torch.empty(0, h, D, dtype=torch.bfloat16, device=DEV)
+        prefix = None
+    g = torch.Generator(device=DEV).manual_seed(33)
+    q, k, v = (torch.randn(total - start, h, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+    scale = 1 / math.sqrt(D)
+    out = prefill_attention(q, k, v, prefix, layer, segments, start, scale)
+    keys, values = torch.cat([pre_k, k]), torch.cat([pre_v, v])
+    for s0, e, is_image in segments:
+        if e <= start:
+            continue
+        s = max(s0, start)
+        mask = torch.ones(e - s, e, dtype=torch.bool, device=DEV)
+        if not is_image:
+            mask = torch.arange(e, device=DEV)[None, :] <= torch.arange(s, e, device=DEV)[:, None]
+        ref = _sdpa_ref(q[s - start:e - start], keys[:e], values[:e], mask, scale)
+        _check(out[s - start:e - start], None, ref, None)
+
+
+def test_prefill_attention_rejects_a_prefix_ending_inside_an_image():
+    from qwenedit_b200.attention import prefill_attention
+
+    q = torch.zeros(10, 1, D, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError, match="inside an image block"):
+        prefill_attention(q, q, q, None, 0, [(0, 20, True)], 10)
