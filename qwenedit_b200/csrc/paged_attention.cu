@@ -186,6 +186,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 columns issued without waiting; tmem_ld_wait then waits for every load this thread has in flight and, by
+// taking the registers as read-write operands, keeps the compiler from reading them any earlier
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -451,20 +474,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // pass 1: the row's max of the raw scores over the visible keys (S stays in tensor memory, read 32
       // columns at a time; four independent three-input max chains), scaled once afterwards (scale > 0)
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      {
+        uint32_t buf[2][32];
+        tmem_ld32_async(s_col, buf[0]);
+        tmem_ld_wait(buf[0]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float chunk[32];
-        tmem_ld32(s_col + 32 * c, chunk);
-        if (masked) {
+        for (int c = 0; c < 4; ++c) {
+          if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
+          float chunk[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : -INFINITY;
-        }
+          for (int i = 0; i < 32; ++i) chunk[i] = __uint_as_float(buf[c & 1][i]);
+          if (masked) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          m4[0] = max3(m4[0], chunk[i], chunk[i + 1]);
-          m4[1] = max3(m4[1], chunk[i + 2], chunk[i + 3]);
-          m4[2] = max3(m4[2], chunk[i + 4], chunk[i + 5]);
-          m4[3] = max3(m4[3], chunk[i + 6], chunk[i + 7]);
+            for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : -INFINITY;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            m4[0] = max3(m4[0], chunk[i], chunk[i + 1]);
+            m4[1] = max3(m4[1], chunk[i + 2], chunk[i + 3]);
+            m4[2] = max3(m4[2], chunk[i + 4], chunk[i + 5]);
+            m4[3] = max3(m4[3], chunk[i + 6], chunk[i + 7]);
+          }
+          if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
         }
       }
       const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
@@ -494,27 +525,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float nbase = m_use == -INFINITY ? 0.0f : -m_use;
       const f32x2 scale2 = pk2(p.scale_log2, p.scale_log2), nbase2 = pk2(nbase, nbase);
       f32x2 l4[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
+      {
+        uint32_t buf[2][32];
+        tmem_ld32_async(s_col, buf[0]);
+        tmem_ld_wait(buf[0]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float chunk[32];
-        uint32_t w[16];
-        tmem_ld32(s_col + 32 * c, chunk);
+        for (int c = 0; c < 4; ++c) {
+          if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
+          float chunk[32];
+          uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 x = up2(fma2(pk2(chunk[2 * i], chunk[2 * i + 1]), scale2, nbase2));
-          chunk[2 * i] = ex2(x.x);
-          chunk[2 * i + 1] = ex2(x.y);
+          for (int i = 0; i < 16; ++i) {
+            const float2 x = up2(fma2(pk2(__uint_as_float(buf[c & 1][2 * i]), __uint_as_float(buf[c & 1][2 * i + 1])),
+                                      scale2, nbase2));
+            chunk[2 * i] = ex2(x.x);
+            chunk[2 * i + 1] = ex2(x.y);
+          }
+          if (masked) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            l4[i & 3] = add2(l4[i & 3], pk2(chunk[2 * i], chunk[2 * i + 1]));
+            w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
+          }
+          tmem_st16(s_col + 16 * c, w);  // columns 16c .. 16c + 15: already read, not those in flight
+          if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
         }
-        if (masked) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          l4[i & 3] = add2(l4[i & 3], pk2(chunk[2 * i], chunk[2 * i + 1]));
-          w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
-        }
-        tmem_st16(s_col + 16 * c, w);
       }
       {
         const float2 a = up2(add2(add2(l4[0], l4[1]), add2(l4[2], l4[3])));
