@@ -175,6 +175,12 @@ int qe_set_silu_table_mode(int32_t mode);
  * T = 32768). No counterpart in the reference. */
 int qe_set_nvfp4_numerics(int32_t numerics);
 
+/* Launch of qe_norm_scale_fp4 / qe_silu_mul_fp4 and their amax modes (process-wide): 1 (default) = with
+ * programmatic stream serialization, so that the next kernel on the stream may place its CTAs on SMs this launch has
+ * left while its last CTAs run (each quantiser waits for the grids it depends on before its first global read);
+ * 0 = plain stream order. Results are identical. No counterpart in the reference; for measurement. */
+int qe_set_nvfp4_pdl(int32_t on);
+
 /* SiLU kernel load schedule (process-wide): 0 = load then compute (1024 threads per CTA); 1 = the next item's
  * loads issued before the current one is computed (1024 threads; default); 2 = the same with two items per
  * iteration (512 threads). Results are identical. No counterpart in the reference. */

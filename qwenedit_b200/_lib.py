@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "qe_set_silu_table_mode": [c_int32],
     "qe_set_silu_pipeline": [c_int32],
     "qe_set_nvfp4_numerics": [c_int32],
+    "qe_set_nvfp4_pdl": [c_int32],
     "qe_paged_attention": [c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                            c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
                            c_float, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],

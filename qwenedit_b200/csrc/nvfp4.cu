@@ -290,6 +290,17 @@ __device__ __forceinline__ void zero_sf_row(uint8_t *sf, int64_t m, int64_t K, i
   for (int g = lane * 4; g < int(K / 16); g += 128) *reinterpret_cast<uint32_t *>(sf + sf_offset(m, g, K)) = 0u;
 }
 
+// ---- programmatic dependent launch ------------------------------------------------------------------
+// The quantisers are launched so that the next kernel on the stream may start its CTAs while this one's last
+// CTAs finish (cudaLaunchAttributeProgrammaticStreamSerialization). Before its first global read a kernel waits
+// for the grids it depends on to complete and their writes to be visible (griddepcontrol.wait; a no-op when it
+// was launched without the attribute), and it allows its own dependents to launch right away
+// (griddepcontrol.launch_dependents): they take SMs only as this kernel's CTAs leave them.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- RMSNorm + adaLN -> NVFP4 ------------------------------------------------------------------
 struct NormParams {
   const uint4 *x;
@@ -454,6 +465,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   // rows (to within one per warp slot) whatever M is
   const int64_t warp0 = int64_t(wid) * gridDim.x + blockIdx.x;
   const int64_t nwarps = int64_t(gridDim.x) * kWarps;
+  pdl_enter();
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
   const float kf = float(K);
   if (!kAmax) build_scale_table(scale_tab, gs, p.numerics);
@@ -722,6 +734,25 @@ __global__ void __launch_bounds__(kWarps * 32) norm_scale_fp4_kernel(NormParams 
   }
 }
 
+// 1: launch the quantisers with programmatic stream serialization (default); 0: plain stream order
+std::atomic<int> g_nvfp4_pdl{1};
+
+template <typename Params>
+cudaError_t launch_pdl(void (*kernel)(Params), unsigned blocks, unsigned threads, size_t smem, cudaStream_t stream,
+                       const Params &p) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_nvfp4_pdl.load(std::memory_order_relaxed) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <int kK, int kWarps, int kTab, bool kShift, bool kAmax>
 int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   auto kernel = norm_scale_fp4_kernel<kK, kWarps, kTab, kShift, kAmax>;
@@ -740,8 +771,8 @@ int launch_norm_typed(const NormParams &p, size_t smem, cudaStream_t stream) {
   if (kTab == 2 && occ > int(512 / kTmemCols)) occ = int(512 / kTmemCols);
   const int64_t blocks_needed = (p.padded + kWarps - 1) / kWarps;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(blocks_needed, int64_t(sm_count()) * occ));
-  kernel<<<dim3(unsigned(blocks)), dim3(kWarps * 32), smem, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "qe_norm_scale_fp4 launch");
+  return cuda_status(launch_pdl(kernel, unsigned(blocks), unsigned(kWarps * 32), smem, stream, p),
+                     "qe_norm_scale_fp4 launch");
 }
 
 template <int kK, int kTab, bool kShift, bool kAmax>
@@ -871,6 +902,7 @@ __global__ void __launch_bounds__(silu_threads(kSched), 1) silu_mul_fp4_kernel(S
   constexpr int kItems = silu_items(kSched);
   extern __shared__ uint4 tab4[];
   float *scale_tab = reinterpret_cast<float *>(tab4 + (kL1 ? 0 : kSiluTable / 8));
+  pdl_enter();
   if (!kL1)
     for (int i = threadIdx.x; i < kSiluTable / 8; i += kThreads) tab4[i] = __ldg(p.table + i);
   const float gs = kAmax ? 1.0f : __ldg(p.gs);
@@ -1129,6 +1161,12 @@ int qe_set_nvfp4_numerics(int32_t numerics) {
   return qe::ok();
 }
 
+int qe_set_nvfp4_pdl(int32_t on) {
+  if (on != 0 && on != 1) return fail(QE_ERR_INVALID, "qe_set_nvfp4_pdl: 0 or 1");
+  qe::g_nvfp4_pdl.store(on, std::memory_order_relaxed);
+  return qe::ok();
+}
+
 int qe_set_norm_table_mode(int32_t mode) {
   if (mode < 0 || mode > 2) return fail(QE_ERR_INVALID, "qe_set_norm_table_mode: mode must be 0, 1 or 2");
   qe::g_norm_table_mode.store(mode, std::memory_order_relaxed);
@@ -1207,8 +1245,7 @@ int silu_mul_impl(const void *gate, const void *value, const float *gs, int64_t 
   const int64_t pad_items = amax ? 0 : (padded - M) * (K / 64) / 32;
   int64_t blocks = (std::max<int64_t>(items, pad_items) + warps_per_block - 1) / warps_per_block;
   blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count())));
-  kernel<<<dim3(unsigned(blocks)), dim3(threads), smem, st>>>(p);
-  return cuda_status(cudaGetLastError(), "qe_silu_mul_fp4 launch");
+  return cuda_status(launch_pdl(kernel, unsigned(blocks), unsigned(threads), smem, st, p), "qe_silu_mul_fp4 launch");
 }
 }  // namespace
 }  // namespace qe
