@@ -259,14 +259,18 @@ struct HeadsParams {
   int64_t pool_rows, n_tokens, row_bytes, head_bytes, out_head_stride, out_token_stride;
   const int64_t *slots;
   int32_t n_planes, rows_per_pass;
+  int32_t head_shift;  // log2(head_bytes / 16) when that is a power of two, else -1
   int32_t *err;
 };
 
-__global__ void __launch_bounds__(kThreads) gather_heads_kernel(HeadsParams p) {
+// Loads of a pass first (16 vectors per lane, a validity bitmask), then a second walk over the same vectors
+// for their head-major destinations, so no destination pointer is kept live across the loads; the head of a
+// vector is a shift when the head size is a power of two (head_shift >= 0).
+__global__ void __launch_bounds__(kThreads, 2) gather_heads_kernel(HeadsParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * kThreads) >> 5;
-  const int64_t vpr = p.row_bytes / 16, vph = p.head_bytes / 16;
+  const int vpr = int(p.row_bytes / 16), vph = int(p.head_bytes / 16);
   const int R = p.rows_per_pass;
   const int64_t blocks_per_plane = (p.n_tokens + R - 1) / R;
   const int64_t items = int64_t(p.n_planes) * blocks_per_plane;
@@ -282,22 +286,17 @@ __global__ void __launch_bounds__(kThreads) gather_heads_kernel(HeadsParams p) {
       }
     }
     const char *pool_plane = p.pool.plane(plane);
-    char *out_plane = p.out.plane(plane);
-    for (int64_t base = 0; base < int64_t(R) * vpr; base += 32 * kRowsUnroll) {
-      // (row, head, vector-in-head) of vector base + lane, advanced by 32 per k
-      int64_t v = base + lane;
-      int ri = int(v / vpr);
-      int64_t vin = v - int64_t(ri) * vpr;
+    char *out_plane = p.out.plane(plane) + t0 * p.out_token_stride;
+    for (int base = 0; base < R * vpr; base += 32 * kRowsUnroll) {
       int4 buf[kRowsUnroll];
-      int4 *dst_at[kRowsUnroll];
+      uint32_t valid = 0u;
+      int ri = (base + lane) / vpr, vin = (base + lane) - ri * vpr;
 #pragma unroll
       for (int k = 0; k < kRowsUnroll; ++k) {
         const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
-        dst_at[k] = nullptr;
         if (ri < R && slot >= 0) {
-          const int64_t h = vin / vph, w = vin - h * vph;
+          valid |= 1u << k;
           buf[k] = ld_stream(reinterpret_cast<const int4 *>(pool_plane + slot * p.row_bytes) + vin);
-          dst_at[k] = reinterpret_cast<int4 *>(out_plane + h * p.out_head_stride + (t0 + ri) * p.out_token_stride) + w;
         }
         vin += 32;
         while (vin >= vpr) {
@@ -305,9 +304,21 @@ __global__ void __launch_bounds__(kThreads) gather_heads_kernel(HeadsParams p) {
           ++ri;
         }
       }
+      ri = (base + lane) / vpr;
+      vin = (base + lane) - ri * vpr;
 #pragma unroll
       for (int k = 0; k < kRowsUnroll; ++k) {
-        if (dst_at[k]) *dst_at[k] = buf[k];
+        if (valid & (1u << k)) {
+          const int h = p.head_shift >= 0 ? vin >> p.head_shift : vin / vph;
+          const int w = vin - h * vph;
+          *(reinterpret_cast<int4 *>(out_plane + h * p.out_head_stride + int64_t(ri) * p.out_token_stride) + w) =
+              buf[k];
+        }
+        vin += 32;
+        while (vin >= vpr) {
+          vin -= vpr;
+          ++ri;
+        }
       }
     }
   }
@@ -796,10 +807,13 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
   p.slots = slots;
   p.n_planes = n_planes;
   p.rows_per_pass = int32_t(std::max<int64_t>(1, std::min<int64_t>(32 * qe::kRowsUnroll / (row_bytes / 16), 32)));
+  p.head_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((int64_t(1) << sh) == head_bytes / 16) p.head_shift = sh;
   p.err = err_flag;
   const int64_t items = int64_t(n_planes) * ((n_tokens + p.rows_per_pass - 1) / p.rows_per_pass);
   const int64_t warps_per_block = qe::kThreads / 32;
-  int64_t blocks = std::min<int64_t>((items + warps_per_block - 1) / warps_per_block, int64_t(qe::sm_count()) * 8);
+  int64_t blocks = std::min<int64_t>((items + warps_per_block - 1) / warps_per_block, int64_t(qe::sm_count()) * 2);
   blocks = std::max<int64_t>(blocks, 1);
   qe::gather_heads_kernel<<<dim3(unsigned(blocks)), dim3(qe::kThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
   int s = qe::cuda_status(cudaGetLastError(), "qe_gather_slots_heads launch");
