@@ -482,11 +482,23 @@ def encoder_extras(device, peak):
 
     tail_ms = _time_graph([ours])
     tail_ref_ms = _time_graph([reference_ops])
+    # steady state: 8 prompts' gathers back to back from one CUDA graph, each prompt's own scattered slots and
+    # output (0.94 GB of K/V in total, > L2), so every launch reads HBM and no launch latency is in the time
+    prompts = [pool.alloc(n) for _ in range(8)]
+    outs = [torch.empty_like(out_kv) for _ in prompts]
+    kv_ss_ms = _time_graph([lambda s_=s_, o=o: pool.gather_into(s_, o) for s_, o in zip(prompts, outs)])
+    hid_ss_ms = _time_graph([lambda s_=s_: pool.gather_extra(s_) for s_ in prompts])
     if pool.device_errors():
         raise RuntimeError("encoder gather reported an error")
     return {"kv_gather_ms": round(kv_ms, 4), "kv_GB/s": round(kv_bytes / kv_ms / 1e6, 1),
             "hidden_gather_ms": round(hid_ms, 4), "hidden_GB/s": round(hid_bytes / hid_ms / 1e6, 1),
             "bytes": {"kv": kv_bytes, "hidden": hid_bytes}, "note": "single launches: launch latency included",
+            "steady_state": {"kv_gather_ms": round(kv_ss_ms, 4), "kv_GB/s": round(kv_bytes / kv_ss_ms / 1e6, 1),
+                             "kv_frac_of_measured_hbm": round(kv_bytes / kv_ss_ms / 1e6 / peak, 4),
+                             "hidden_gather_ms": round(hid_ss_ms, 4),
+                             "hidden_GB/s": round(hid_bytes / hid_ss_ms / 1e6, 1),
+                             "hidden_frac_of_measured_hbm": round(hid_bytes / hid_ss_ms / 1e6 / peak, 4),
+                             "timing": "8 prompts back to back from one CUDA graph, per-launch mean"},
             "partial_hit_prefix_ms": {"gather_heads_plus_tail_writes": round(tail_ms, 4),
                                       "gather_then_per_layer_transpose_cat": round(tail_ref_ms, 4),
                                       "prefix_tokens": n, "tail_tokens": tail, "timing": "CUDA graph, device time"}}
