@@ -37,6 +37,9 @@ class MTCaches(list):
         self.prefix_lengths = prefix_lengths
         self.prepared = False
         self.matches: list[Match] = []
+        # sample -> PagedPrefix: full hits served without a gather (fill_from_pool(paged=True)); the attention
+        # reads them through qwenedit_b200.attention.paged_attention
+        self.paged: dict = {}
 
     def release(self) -> None:
         for match in self.matches:
@@ -56,15 +59,56 @@ def set_caches(caches, sample: int, kv: torch.Tensor) -> None:
 # prefill(sample, kv, start): fill kv[:, :, start:] ([L, 2, total, H, D]) for prefix positions start.. of `sample`
 Prefill = Callable[[int, torch.Tensor, int], None]
 
+FULL, PARTIAL, MISS = "full", "partial", "miss"
 
-def fill_from_pool(pool: PagedKVPool, caches: MTCaches, prefill: Prefill | None = None) -> list[int]:
-    """Serve each sample's prefix from the pool; returns the samples that missed (to store after the forward).
 
-    * full hit: the prefix is gathered once (a view when the slots are one run) and kept locked;
-    * partial hit of at least MULTI_TURN_MIN_REUSE tokens: the head is gathered into a fresh [L, 2, total, H, D]
-      buffer, `prefill` computes the tail, and the tail is appended and inserted (owned from the match);
-    * otherwise: a miss.
-    """
+def classify(matched: int, total: int, can_prefill: bool) -> str:
+    """How a sample's prefix is served given the matched length: the whole prefix cached (FULL); enough of it
+    cached to be worth a tail prefill, at least MULTI_TURN_MIN_REUSE tokens, when the caller can prefill (PARTIAL);
+    otherwise computed from scratch (MISS). The reference's branch rule (hooks.py:99-123)."""
+    if matched == total:
+        return FULL
+    if can_prefill and matched >= state.MIN_REUSE:
+        return PARTIAL
+    return MISS
+
+
+def _serve_full(pool: PagedKVPool, caches: MTCaches, sample: int, match: Match, paged: bool) -> None:
+    # the gathered prefix (a view when its slots are one run), or the pages themselves, stay valid while the match
+    # holds its lock
+    if paged:
+        from qwenedit_b200.attention import PagedPrefix
+
+        caches.paged[sample] = PagedPrefix(pool, match.indices)
+    else:
+        set_caches(caches, sample, pool.gather(match.indices))
+    caches.matches.append(match)
+
+
+def _serve_partial(pool: PagedKVPool, caches: MTCaches, sample: int, match: Match, vids, total: int,
+                   prefill: Prefill) -> None:
+    m = match.length
+    kv = torch.empty(pool.layers, 2, total, pool.heads, pool.head_dim, device=pool.kv.device, dtype=pool.kv.dtype)
+    pool.gather_into(match.indices, kv[:, :, :m])
+    prefill(sample, kv, m)
+    set_caches(caches, sample, kv)
+    tail = pool.alloc(total - m)
+    if tail is not None:  # pool full of locked prefixes: serve this request, cache nothing
+        pool.write(tail, kv[:, :, m:])
+        pool.insert(vids, cat_slots(match.indices, tail), owned_from=m)
+    match.release()  # the fresh buffer owns the data now
+
+
+def fill_from_pool(pool: PagedKVPool, caches: MTCaches, prefill: Prefill | None = None, paged: bool = False) -> list[int]:
+    """Serve each sample's prefix from the pool (hooks.py:86-123); returns the samples that missed, to be stored
+    after the forward by `store_computed`.
+
+    FULL: the prefix is gathered once and its match kept locked until the request ends (with `paged`, on a
+    page-mode pool: not gathered at all; `caches.paged[sample]` is a PagedPrefix the attention reads the pages
+    through); PARTIAL: the cached head goes into a fresh [L, 2, total, H, D] buffer, `prefill` computes the tail
+    into it, and the tail is appended and inserted (owned from the match); MISS: nothing reused."""
+    if paged and pool.page_size == 1:
+        raise ValueError("paged serving needs a page-mode pool (page_size 8 or more)")
     pending = []
     for sample, vids in enumerate(caches.vids):
         if vids is None:
@@ -72,28 +116,18 @@ def fill_from_pool(pool: PagedKVPool, caches: MTCaches, prefill: Prefill | None 
         t0 = time.perf_counter()
         total = caches.prefix_lengths[sample]
         match = pool.match(vids)
-        m = match.length
-        if m == total:
-            set_caches(caches, sample, pool.gather(match.indices))
-            caches.matches.append(match)
-        elif m >= state.MIN_REUSE and prefill is not None:
-            kv = torch.empty(pool.layers, 2, total, pool.heads, pool.head_dim, device=pool.kv.device,
-                             dtype=pool.kv.dtype)
-            pool.gather_into(match.indices, kv[:, :, :m])
-            prefill(sample, kv, m)
-            set_caches(caches, sample, kv)
-            slots = pool.alloc(total - m)
-            if slots is not None:
-                pool.write(slots, kv[:, :, m:])
-                pool.insert(vids, cat_slots(match.indices, slots), owned_from=m)
-            match.release()
+        kind = classify(match.length, total, prefill is not None)
+        reused = match.length if kind != MISS else 0
+        if kind == FULL:
+            _serve_full(pool, caches, sample, match, paged)
+        elif kind == PARTIAL:
+            _serve_partial(pool, caches, sample, match, vids, total, prefill)
         else:
             match.release()
             pending.append(sample)
-            m = 0
         if state.DEBUG:
-            logger.info("qwenedit_b200: dit sample %d reused %d/%d prefix tokens in %.1f ms", sample, m, total,
-                        (time.perf_counter() - t0) * 1e3)
+            logger.info("qwenedit_b200: dit sample %d (%s) reused %d/%d prefix tokens in %.1f ms", sample, kind,
+                        reused, total, (time.perf_counter() - t0) * 1e3)
     return pending
 
 
@@ -156,4 +190,5 @@ def compose(spec: dict, crop_latents: torch.Tensor, crop_grid: tuple[int, int]) 
     return True
 
 
-__all__ = ["MTCaches", "set_caches", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store", "compose"]
+__all__ = ["MTCaches", "set_caches", "classify", "fill_from_pool", "store_computed", "encoder_hit", "encoder_store",
+           "compose"]

@@ -113,3 +113,39 @@ def test_encoder_store_and_hit():
     assert m.length == 350
     assert torch.equal(hooks.encoder_hit(enc, m, 350), torch.cat([hidden, h2]))
     m.release()
+
+
+def test_full_hit_served_as_pages_feeds_the_paged_attention():
+    """fill_from_pool(paged=True) on a page-mode pool: a full hit is not gathered; the attention over the
+    PagedPrefix equals the attention over the per-layer caches the gathered path would have set."""
+    import math
+
+    from qwenedit_b200.attention import paged_attention
+
+    pool = _pool(4000, 64)
+    total = 640
+    vids = np.arange(1, total + 1, dtype=np.int64)
+    layers = _computed(total, 5)
+    caches = hooks.MTCaches([[LayerCache() for _ in range(L)]], [vids], [total])
+    assert hooks.fill_from_pool(pool, caches, paged=True) == [0]
+    caches[0] = layers
+    hooks.store_computed(pool, caches, [0])
+    caches.release()
+    gathers = pool.stats.gathers
+    caches = hooks.MTCaches([[LayerCache() for _ in range(L)]], [vids], [total])
+    assert hooks.fill_from_pool(pool, caches, paged=True) == []
+    assert pool.stats.gathers == gathers and pool.stats.contiguous_views == 0  # nothing gathered
+    prefix = caches.paged[0]
+    g = torch.Generator(device=DEV).manual_seed(6)
+    q, k, v = (torch.randn(256, H, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+    for layer in (0, L - 1):
+        out = paged_attention(q, prefix, layer, k, v)
+        keys = torch.cat([layers[layer]["key"][0], k]).float().transpose(0, 1)
+        values = torch.cat([layers[layer]["value"][0], v]).float().transpose(0, 1)
+        s = q.float().transpose(0, 1) @ keys.transpose(1, 2) / math.sqrt(D)
+        ref = (torch.softmax(s, dim=-1) @ values).transpose(0, 1)
+        assert (out.float() - ref).abs().max().item() < 2e-2
+    caches.release()
+    assert pool.usage()["protected"] == 0
+    with pytest.raises(ValueError, match="page-mode"):
+        hooks.fill_from_pool(_pool(100), hooks.MTCaches([[LayerCache()]], [vids[:10]], [10]), paged=True)
