@@ -236,6 +236,23 @@ int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_str
                        int32_t causal, float scale, void *out, int64_t out_token_stride, int64_t out_head_stride,
                        float *lse, int32_t *err_flag, void *stream);
 
+/* qe_paged_attention with the own tokens appended to the pool in the same launch: the arguments of
+ * qe_paged_attention plus append_table, device int32 page ids, ceil(n_local / page_size) of them; own token t
+ * (row t of k_local / v_local) is written to pool row append_table[t / page_size] * page_size + t % page_size of
+ * k_pool and v_pool (page_size and the pool planes as above; block_table may be null when n_prefix == 0).
+ * Rows of the last page past own token n_local - 1 are not written. One CTA per K/V head stores the K and V tiles
+ * it has loaded for the attention, so the own K/V are read from HBM once for both. Pages outside the pool are
+ * skipped and set bit 1 of *err_flag (err_flag must not be null). Needs n_q >= 1 and n_local >= 1. Replaces the
+ * separate store of freshly computed prefix K/V after the forward (multi_turn/cache/prefill.py:69-72, the
+ * encoder's _store, multi_turn/cache/encoder.py:131-138); no counterpart as one operation in the reference. */
+int qe_paged_attention_append(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,
+                              int32_t heads_q, const void *k_pool, const void *v_pool, int64_t pool_rows,
+                              int32_t heads_kv, const int32_t *block_table, int32_t page_size, int32_t n_prefix,
+                              const void *k_local, const void *v_local, int64_t local_token_stride,
+                              int64_t local_head_stride, int32_t n_local, int32_t causal, float scale, void *out,
+                              int64_t out_token_stride, int64_t out_head_stride, float *lse,
+                              const int32_t *append_table, int32_t *err_flag, void *stream);
+
 /* ---- head-sharded pools across the GPUs of one node ------------------------------------------
  *
  * No counterpart in the reference, which keeps a prefix on one GPU and disables the pool under tensor or

@@ -69,6 +69,10 @@ SIGNATURES: dict[str, list] = {
     "qe_paged_attention": [c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                            c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
                            c_float, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "qe_paged_attention_append": [c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int64,
+                                  c_int32, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int32,
+                                  c_int32, c_float, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                  c_void_p],
     "qe_norm_scale_amax": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p],
     "qe_silu_mul_amax": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],

@@ -57,13 +57,19 @@ def _check(name: str, t: torch.Tensor | None, device) -> None:
 
 def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0, k_local: torch.Tensor | None = None,
                     v_local: torch.Tensor | None = None, causal: bool = False, scale: float | None = None,
-                    out: torch.Tensor | None = None, return_lse: bool = False):
+                    out: torch.Tensor | None = None, return_lse: bool = False, append: PagedPrefix | None = None):
     """softmax(q K^T * scale) V with K, V = [prefix K/V of `layer` from the pool; k_local / v_local].
 
     q [n_q, Hq, 128] bf16; k_local / v_local [n_local, Hkv, 128] bf16 (the step's own keys, may be None);
     Hq a multiple of the pool's Hkv (grouped-query heads); `causal`: query i sees every prefix key and own keys
     j <= i + n_local - n_q (bottom-right alignment). Returns out [n_q, Hq, 128] bf16 (and the log-sum-exp
-    [Hq, n_q] fp32 of the scaled scores with `return_lse`). One kernel launch on the current stream."""
+    [Hq, n_q] fp32 of the scaled scores with `return_lse`). One kernel launch on the current stream.
+
+    `append`: the pool slots of the own tokens (a PagedPrefix over ``pool.alloc(n_local)``, whole pages of a
+    page-mode pool); the same launch also writes k_local / v_local into layer `layer` of those slots, from the
+    tiles it loads for the attention (the store that cache/prefill.py:69-72 and the encoder's _store,
+    cache/encoder.py:131-138, do as separate copies). Rows of the last page past the last own token are not
+    written."""
     if q.dim() != 3:
         raise ValueError("q must be [tokens, heads, 128]")
     device = q.device
@@ -77,8 +83,14 @@ def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0,
     if k_local is not None and k_local.stride() != v_local.stride():
         raise ValueError("k_local and v_local must have the same strides")
     n_prefix = 0 if prefix is None else prefix.length
-    if prefix is not None:
-        pool = prefix.pool
+    if append is not None:
+        if k_local is None or append.length != n_local:
+            raise ValueError(f"append holds {append.length} slots for {n_local} own tokens")
+        if prefix is not None and append.pool is not prefix.pool:
+            raise ValueError("append and prefix must be slots of the same pool")
+    pool_of = prefix if prefix is not None else append
+    if pool_of is not None:
+        pool = pool_of.pool
         heads_kv = pool.heads
         if pool.head_dim != HEAD_DIM or pool.kv.dtype != torch.bfloat16 or pool.device != device:
             raise ValueError(f"the pool must hold bf16 heads of {HEAD_DIM} on {device}")
@@ -101,11 +113,11 @@ def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0,
     lse = torch.empty(heads_q, n_q, dtype=torch.float32, device=device) if return_lse else None
     scale = 1.0 / math.sqrt(HEAD_DIM) if scale is None else float(scale)
     e = 2
-    if prefix is not None and n_prefix:
-        kp, vp = prefix.planes(layer)
+    if (prefix is not None and n_prefix) or append is not None:
+        kp, vp = pool_of.planes(layer)
         err = pool._err
-        args_pool = (kp.data_ptr(), vp.data_ptr(), pool.rows, heads_kv, prefix.block_table.data_ptr(),
-                     pool.page_size, n_prefix)
+        table = prefix.block_table.data_ptr() if prefix is not None and n_prefix else None
+        args_pool = (kp.data_ptr(), vp.data_ptr(), pool.rows, heads_kv, table, pool.page_size, n_prefix)
     else:
         err = None
         args_pool = (None, None, 0, heads_kv, None, 1, 0)
@@ -113,11 +125,16 @@ def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0,
         args_local = (k_local.data_ptr(), v_local.data_ptr(), k_local.stride(0) * e, k_local.stride(1) * e, n_local)
     else:
         args_local = (None, None, 0, 0, 0)
+    tail = (out.data_ptr(), out.stride(0) * e, out.stride(1) * e, None if lse is None else lse.data_ptr())
     with _lib.on_device(device):
-        _lib.call("qe_paged_attention", q.data_ptr(), q.stride(0) * e, q.stride(1) * e, n_q, heads_q, *args_pool,
-                  *args_local, 1 if causal else 0, scale, out.data_ptr(), out.stride(0) * e, out.stride(1) * e,
-                  None if lse is None else lse.data_ptr(), None if err is None else err.data_ptr(),
-                  _lib.stream_of(device))
+        if append is None:
+            _lib.call("qe_paged_attention", q.data_ptr(), q.stride(0) * e, q.stride(1) * e, n_q, heads_q, *args_pool,
+                      *args_local, 1 if causal else 0, scale, *tail, None if err is None else err.data_ptr(),
+                      _lib.stream_of(device))
+        else:
+            _lib.call("qe_paged_attention_append", q.data_ptr(), q.stride(0) * e, q.stride(1) * e, n_q, heads_q,
+                      *args_pool, *args_local, 1 if causal else 0, scale, *tail, append.block_table.data_ptr(),
+                      err.data_ptr(), _lib.stream_of(device))
     return (out, lse) if return_lse else out
 
 

@@ -66,6 +66,10 @@ constexpr int kSmemBytes = kAbortOff + 4 + 1024;  // + slack to align the base
 struct AttnParams {
   const int32_t *block_table;
   int32_t page_size, n_prefix, prefix_tiles, pool_pages, last_page, tail_rows;
+  // fused append of the own K/V tiles into the pool (qe_paged_attention_append): the own tokens' page ids, the
+  // index of their last page and its valid rows; null when not appending
+  const int32_t *append_table;
+  int32_t append_last_page, append_tail_rows;
   int32_t n_q, n_local, heads_q, group, causal;
   float scale_log2;
   __nv_bfloat16 *out;
@@ -128,6 +132,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
+// shared -> global tensor store (bulk group); rows outside the map's extents are not written
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int32_t c0, int32_t c1, int32_t c2,
+                                             int32_t c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
                                             int32_t c3, uint32_t bar) {
   asm volatile(
@@ -267,11 +282,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// Own-key tiles query-tile CTA x reads: all of them, or under the causal mask those up to the last own key its
+// last query sees.
+__device__ __forceinline__ int own_key_tiles(const AttnParams &p, int x) {
+  if (p.n_local <= 0) return 0;
+  int last_key = p.n_local - 1;
+  if (p.causal) last_key = min(last_key, min((x + 1) * kQTiles * kTile, p.n_q) - 1 + p.n_local - p.n_q);
+  return last_key >= 0 ? last_key / kTile + 1 : 0;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     paged_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kpool,
                            const __grid_constant__ CUtensorMap tm_vpool, const __grid_constant__ CUtensorMap tm_ktail,
                            const __grid_constant__ CUtensorMap tm_vtail, const __grid_constant__ CUtensorMap tm_klocal,
-                           const __grid_constant__ CUtensorMap tm_vlocal, const AttnParams p) {
+                           const __grid_constant__ CUtensorMap tm_vlocal, const __grid_constant__ CUtensorMap tm_kapp,
+                           const __grid_constant__ CUtensorMap tm_vapp, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -285,12 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hq = blockIdx.y;
   const int hkv = hq / p.group;
   // key tiles: the prefix's, then the visible ones of the step's own keys
-  int local_tiles = 0;
-  if (p.n_local > 0) {
-    int last_key = p.n_local - 1;
-    if (p.causal) last_key = min(last_key, min(q0 + kQTiles * kTile, p.n_q) - 1 + p.n_local - p.n_q);
-    local_tiles = last_key >= 0 ? last_key / kTile + 1 : 0;
-  }
+  const int local_tiles = own_key_tiles(p, blockIdx.x);
   const int n_tiles = p.prefix_tiles + local_tiles;
 
   if (threadIdx.x == 0) {
@@ -365,19 +385,66 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(dst + h * kHalfBytes, is_v ? &tm_vlocal : &tm_klocal, h * 64, hkv, l0, full);
         }
       };
-      bool ok = true;
+      // Fused append: each own K/V tile j is stored into the pool pages of the own tokens (the last page through
+      // a map whose row extent ends at the last token, so nothing past it is written) by exactly one of the CTAs
+      // that load it: r = j mod (query-tile CTAs x group) names a query head of the group (r / G) and a query-tile
+      // CTA (r mod G); under the causal mask, when that CTA does not load tile j, the first CTA that does stores
+      // it (the loaded own tiles grow with the query tile). A stage is reloaded only after its stores read it.
+      auto stores_tile = [&](int it) -> bool {
+        if (p.append_table == nullptr || it < p.prefix_tiles) return false;
+        const int G = int(gridDim.x);
+        const int j = it - p.prefix_tiles;
+        const int r = j % (G * p.group);
+        if (hq % p.group != r / G) return false;
+        const int xc = r % G, x = int(blockIdx.x);
+        if (xc == x) return true;
+        return xc < x && j >= own_key_tiles(p, x - 1);
+      };
+      auto store_tile = [&](int it, uint32_t src, bool is_v) {
+        const CUtensorMap *full_map = is_v ? &tm_vpool : &tm_kpool;
+        const CUtensorMap *tail_map = is_v ? &tm_vapp : &tm_kapp;
+        const int l0 = (it - p.prefix_tiles) * kTile;
+        const int rows = P >= kTile ? kTile : P;
+        for (int sub = 0; sub < kTile / rows; ++sub) {
+          const int key = l0 + sub * rows;
+          if (key >= p.n_local) break;
+          const int pi = key / P;
+          const int page = __ldg(p.append_table + pi);
+          if (page < 0 || page >= p.pool_pages) {
+            if (p.err) atomicOr(p.err, 1);
+            continue;
+          }
+          const CUtensorMap *map = pi == p.append_last_page ? tail_map : full_map;
+          for (int h = 0; h < 2; ++h)
+            tma_store_4d(map, src + h * kHalfBytes + sub * rows * 128, h * 64, hkv, key % P, page);
+        }
+      };
+      bool ok = true, stored = false;
       for (int it = 0; it < n_tiles && ok; ++it) {
         const int s = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         ok = mbar_wait(bar(kKEmpty + s), ph ^ 1, abort, p.err);
         if (!ok) break;
+        if (stored) {  // the stores of an earlier tile may still read this stage
+          bulk_wait_read_all();
+          stored = false;
+        }
         mbar_expect_tx(bar(kKFull + s), kTileBytes);
         load_tile(it, sbase + kKOff + s * kTileBytes, false, bar(kKFull + s));
         ok = mbar_wait(bar(kVEmpty + s), ph ^ 1, abort, p.err);
         if (!ok) break;
         mbar_expect_tx(bar(kVFull + s), kTileBytes);
         load_tile(it, sbase + kVOff + s * kTileBytes, true, bar(kVFull + s));
+        if (stores_tile(it)) {
+          ok = mbar_wait(bar(kKFull + s), ph, abort, p.err) && mbar_wait(bar(kVFull + s), ph, abort, p.err);
+          if (!ok) break;
+          store_tile(it, sbase + kKOff + s * kTileBytes, false);
+          store_tile(it, sbase + kVOff + s * kTileBytes, true);
+          bulk_commit();
+          stored = true;
+        }
       }
+      if (p.append_table) bulk_wait_all();  // the appended rows are in global memory before the CTA retires
       if (!ok) {  // give the copies already issued time to land before the CTA's shared memory is released
         const uint64_t t0 = globaltimer();
         while (globaltimer() - t0 < 200000ull) {
@@ -637,17 +704,19 @@ bool al16(int64_t v) { return v % 16 == 0; }
 
 using qe::fail;
 
-extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,
-                                  int32_t heads_q, const void *k_pool, const void *v_pool, int64_t pool_rows,
-                                  int32_t heads_kv, const int32_t *block_table, int32_t page_size, int32_t n_prefix,
-                                  const void *k_local, const void *v_local, int64_t local_token_stride,
-                                  int64_t local_head_stride, int32_t n_local, int32_t causal, float scale, void *out,
-                                  int64_t out_token_stride, int64_t out_head_stride, float *lse, int32_t *err_flag,
-                                  void *stream) {
-  using namespace qe;
+namespace qe {
+namespace {
+int paged_attention_impl(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q, int32_t heads_q,
+                         const void *k_pool, const void *v_pool, int64_t pool_rows, int32_t heads_kv,
+                         const int32_t *block_table, int32_t page_size, int32_t n_prefix, const void *k_local,
+                         const void *v_local, int64_t local_token_stride, int64_t local_head_stride, int32_t n_local,
+                         int32_t causal, float scale, void *out, int64_t out_token_stride, int64_t out_head_stride,
+                         float *lse, const int32_t *append_table, int32_t *err_flag, void *stream) {
   QE_CHECK_ARG(n_q >= 0 && n_prefix >= 0 && n_local >= 0, "qe_paged_attention: negative size");
   QE_CHECK_ARG(heads_q >= 1 && heads_kv >= 1 && heads_q % heads_kv == 0 && heads_q <= 65535,
                "qe_paged_attention: heads_q must be a positive multiple of heads_kv (at most 65535)");
+  QE_CHECK_ARG(append_table == nullptr || n_q > 0, "qe_paged_attention_append: no queries (the appending CTAs "
+               "are query-tile CTAs)");
   if (n_q == 0) return ok();
   QE_CHECK_ARG(q && out, "qe_paged_attention: null q or out");
   QE_CHECK_ARG(n_prefix + n_local >= 1, "qe_paged_attention: no keys (n_prefix + n_local == 0)");
@@ -657,8 +726,11 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
                "qe_paged_attention: q / out must be 16-byte aligned with 16-byte multiple strides, rows of 128 bf16");
   QE_CHECK_ARG(std::isfinite(scale) && scale > 0.0f, "qe_paged_attention: scale must be positive and finite");
   int32_t prefix_tiles = 0, pool_pages = 0, last_page = -1, tail_rows = 0;
-  if (n_prefix > 0) {
-    QE_CHECK_ARG(k_pool && v_pool && block_table, "qe_paged_attention: null pool plane or block table");
+  const bool append = append_table != nullptr;
+  QE_CHECK_ARG(!append || n_local > 0, "qe_paged_attention_append: nothing to append (n_local == 0)");
+  if (n_prefix > 0 || append) {
+    QE_CHECK_ARG(k_pool && v_pool && (block_table || n_prefix == 0),
+                 "qe_paged_attention: null pool plane or block table");
     QE_CHECK_ARG(aligned16(k_pool) && aligned16(v_pool), "qe_paged_attention: pool planes must be 16-byte aligned");
     QE_CHECK_ARG(page_size >= 8 && ((kTile % page_size) == 0 || (page_size % kTile) == 0) && page_size <= 1 << 20,
                  "qe_paged_attention: page_size must be a divisor of 128 (>= 8) or a multiple of 128");
@@ -666,15 +738,17 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
                  "qe_paged_attention: pool_rows must be a positive multiple of page_size");
     prefix_tiles = (n_prefix + kTile - 1) / kTile;
     pool_pages = int32_t(pool_rows / page_size);
-    last_page = (n_prefix - 1) / page_size;
-    tail_rows = n_prefix - last_page * page_size;
+    if (n_prefix > 0) {
+      last_page = (n_prefix - 1) / page_size;
+      tail_rows = n_prefix - last_page * page_size;
+    }
   }
   if (n_local > 0) {
     QE_CHECK_ARG(k_local && v_local && aligned16(k_local) && aligned16(v_local) && al16(local_token_stride) &&
                      al16(local_head_stride) && local_token_stride > 0 && local_head_stride >= 256,
                  "qe_paged_attention: local K / V must be 16-byte aligned with 16-byte multiple strides");
   }
-  CUtensorMap maps[7];
+  CUtensorMap maps[9];
   std::memset(maps, 0, sizeof(maps));
   const uint32_t box3[3] = {64, 1, uint32_t(kTile)};
   int s;
@@ -684,7 +758,7 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
     if ((s = make_map(&maps[0], q, 3, dims, strides, box3, "q"))) return s;
   }
   const int64_t row_bytes = int64_t(heads_kv) * kHeadDim * 2;
-  if (n_prefix > 0) {
+  if (n_prefix > 0 || append) {
     const uint32_t box_rows = uint32_t(std::min(page_size, kTile));
     const uint32_t box4[4] = {64, 1, box_rows, 1};
     const uint64_t strides[3] = {uint64_t(kHeadDim * 2), uint64_t(row_bytes), uint64_t(row_bytes * page_size)};
@@ -692,8 +766,17 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
     const uint64_t tail[4] = {uint64_t(kHeadDim), uint64_t(heads_kv), uint64_t(tail_rows), uint64_t(pool_pages)};
     if ((s = make_map(&maps[1], k_pool, 4, full, strides, box4, "the K pool"))) return s;
     if ((s = make_map(&maps[2], v_pool, 4, full, strides, box4, "the V pool"))) return s;
-    if ((s = make_map(&maps[3], k_pool, 4, tail, strides, box4, "the K pool tail"))) return s;
-    if ((s = make_map(&maps[4], v_pool, 4, tail, strides, box4, "the V pool tail"))) return s;
+    if (n_prefix > 0) {
+      if ((s = make_map(&maps[3], k_pool, 4, tail, strides, box4, "the K pool tail"))) return s;
+      if ((s = make_map(&maps[4], v_pool, 4, tail, strides, box4, "the V pool tail"))) return s;
+    }
+    if (append) {  // the own tokens' last page: rows past the last own token are outside the map, never written
+      const int64_t app_last = (int64_t(n_local) - 1) / page_size;
+      const uint64_t app_tail[4] = {uint64_t(kHeadDim), uint64_t(heads_kv),
+                                    uint64_t(int64_t(n_local) - app_last * page_size), uint64_t(pool_pages)};
+      if ((s = make_map(&maps[7], k_pool, 4, app_tail, strides, box4, "the K append tail"))) return s;
+      if ((s = make_map(&maps[8], v_pool, 4, app_tail, strides, box4, "the V append tail"))) return s;
+    }
   }
   if (n_local > 0) {
     const uint64_t dims[3] = {uint64_t(kHeadDim), uint64_t(heads_kv), uint64_t(n_local)};
@@ -709,6 +792,9 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
   p.pool_pages = pool_pages;
   p.last_page = last_page;
   p.tail_rows = tail_rows;
+  p.append_table = append_table;
+  p.append_last_page = append ? (n_local - 1) / page_size : -1;
+  p.append_tail_rows = append ? n_local - p.append_last_page * page_size : 0;
   p.n_q = n_q;
   p.n_local = n_local;
   p.heads_q = heads_q;
@@ -732,7 +818,38 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
   }
   const dim3 grid(unsigned((n_q + kQTiles * kTile - 1) / (kQTiles * kTile)), unsigned(heads_q));
   paged_attention_kernel<<<grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], p);
+      maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], maps[7], maps[8], p);
   s = cuda_status(cudaGetLastError(), "qe_paged_attention launch");
   return s ? s : ok();
+}
+}  // namespace
+}  // namespace qe
+
+extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,
+                                  int32_t heads_q, const void *k_pool, const void *v_pool, int64_t pool_rows,
+                                  int32_t heads_kv, const int32_t *block_table, int32_t page_size, int32_t n_prefix,
+                                  const void *k_local, const void *v_local, int64_t local_token_stride,
+                                  int64_t local_head_stride, int32_t n_local, int32_t causal, float scale, void *out,
+                                  int64_t out_token_stride, int64_t out_head_stride, float *lse, int32_t *err_flag,
+                                  void *stream) {
+  return qe::paged_attention_impl(q, q_token_stride, q_head_stride, n_q, heads_q, k_pool, v_pool, pool_rows, heads_kv,
+                                  block_table, page_size, n_prefix, k_local, v_local, local_token_stride,
+                                  local_head_stride, n_local, causal, scale, out, out_token_stride, out_head_stride, lse,
+                                  nullptr, err_flag, stream);
+}
+
+extern "C" int qe_paged_attention_append(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,
+                                         int32_t heads_q, const void *k_pool, const void *v_pool, int64_t pool_rows,
+                                         int32_t heads_kv, const int32_t *block_table, int32_t page_size,
+                                         int32_t n_prefix, const void *k_local, const void *v_local,
+                                         int64_t local_token_stride, int64_t local_head_stride, int32_t n_local,
+                                         int32_t causal, float scale, void *out, int64_t out_token_stride,
+                                         int64_t out_head_stride, float *lse, const int32_t *append_table,
+                                         int32_t *err_flag, void *stream) {
+  if (!append_table || !err_flag)
+    return qe::fail(QE_ERR_INVALID, "qe_paged_attention_append: null append table or error flag");
+  return qe::paged_attention_impl(q, q_token_stride, q_head_stride, n_q, heads_q, k_pool, v_pool, pool_rows, heads_kv,
+                                  block_table, page_size, n_prefix, k_local, v_local, local_token_stride,
+                                  local_head_stride, n_local, causal, scale, out, out_token_stride, out_head_stride, lse,
+                                  append_table, err_flag, stream);
 }

@@ -184,6 +184,85 @@ def test_strided_views_in_and_out():
     assert bool((wide[:, :h] == 0).all()) and bool((wide[:, 2 * h:] == 0).all())
 
 
+# ---- fused append: the own K/V stored into the pool by the attention launch itself ------------------------------
+APPEND_CASES = [  # (page, heads_q, heads_kv, n_q, n_prefix, n_local, causal, layers, layer)
+    (64, 4, 2, 300, 1000, 300, True, 2, 1),     # GQA, causal, ragged own tokens (4 pages + 44 rows)
+    (16, 2, 2, 257, 0, 257, False, 1, 0),      # first turn (no prefix), pages shorter than a key tile
+    (256, 2, 1, 512, 512, 700, False, 2, 0),   # pages of two key tiles, more own keys than queries
+    (128, 2, 2, 1024, 4096, 1024, False, 1, 0),  # whole pages
+]
+
+
+@pytest.mark.parametrize("case", APPEND_CASES, ids=lambda c: "-".join(map(str, c)))
+def test_fused_append_stores_the_own_tokens(case):
+    """paged_attention(append=...): the output as without the append, and the pool afterwards equal to the pool
+    before with exactly the own tokens' rows of `layer` replaced by k_local / v_local (bit-exact); the rows of
+    the last page past the last own token, the other layers and every other page keep their NaN."""
+    page, hq, hkv, n_q, n_prefix, n_local, causal, layers, layer = case
+    n_app_pages = -(-n_local // page)
+    pool = _pool(layers, hkv, page, -(-n_prefix // page) + n_app_pages + 3, seed=page + 1)
+    slots, vals = _prefix(pool, n_prefix, seed=n_prefix + 1) if n_prefix else (None, None)
+    used = set() if slots is None else set((slots.cpu().numpy() // page).tolist())
+    rng = np.random.default_rng(n_local)
+    free = [p for p in rng.permutation(np.arange(1, pool.rows // page)).tolist() if p not in used]
+    t = np.arange(n_local)
+    app_slots = torch.from_numpy(np.array(free[:n_app_pages])[t // page] * page + t % page).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(17)
+    q = torch.randn(n_q, hq, D, generator=g, device=DEV).bfloat16()
+    kv_own = torch.randn(n_local, 2 * hkv, D, generator=g, device=DEV).bfloat16()
+    k_own, v_own = kv_own[:, :hkv], kv_own[:, hkv:]  # strided token rows, as a fused K/V projection gives them
+    before = pool.kv.clone()
+    prefix = PagedPrefix(pool, slots) if n_prefix else None
+    scale = 1 / math.sqrt(D)
+    out, lse = paged_attention(q, prefix, layer, k_own, v_own, causal=causal, scale=scale, return_lse=True,
+                               append=PagedPrefix(pool, app_slots))
+    torch.cuda.synchronize()
+    assert pool.device_errors() == 0
+    k = k_own if not n_prefix else torch.cat([vals[layer, 0], k_own])
+    v = v_own if not n_prefix else torch.cat([vals[layer, 1], v_own])
+    ref_out, ref_lse = _reference(q, k, v, scale, causal, n_local)
+    _check(out, lse, ref_out, ref_lse)
+    want = before
+    want[layer, 0, app_slots] = k_own
+    want[layer, 1, app_slots] = v_own
+    assert torch.equal(pool.kv.view(torch.int16), want.view(torch.int16))
+
+
+def test_fused_append_skips_a_page_outside_the_pool():
+    page, h, n = 32, 2, 100
+    pool = _pool(1, h, page, 8, seed=21)
+    t = np.arange(n)
+    pages = np.array([2, 5, 3, 6])
+    app = PagedPrefix(pool, torch.from_numpy(pages[t // page] * page + t % page).to(DEV))
+    app.block_table[1] = pool.rows // page + 2  # the second page points past the pool
+    g = torch.Generator(device=DEV).manual_seed(22)
+    q, k_own, v_own = (torch.randn(n, h, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+    before = pool.kv.clone()
+    out = paged_attention(q, None, 0, k_own, v_own, causal=True, append=app)
+    torch.cuda.synchronize()
+    assert pool.device_errors() & 1
+    ref_out, _ = _reference(q, k_own, v_own, 1 / math.sqrt(D), True, n)
+    _check(out, None, ref_out, None)
+    want = before
+    keep = torch.from_numpy(np.r_[0:page, 2 * page:n]).to(DEV)
+    rows = torch.from_numpy((pages[t // page] * page + t % page)[np.r_[0:page, 2 * page:n]]).to(DEV)
+    want[0, 0, rows] = k_own[keep]
+    want[0, 1, rows] = v_own[keep]
+    assert torch.equal(pool.kv.view(torch.int16), want.view(torch.int16))
+
+
+def test_fused_append_argument_checks():
+    pool = _pool(1, 2, 64, 4, seed=23)
+    q = torch.zeros(64, 2, D, dtype=torch.bfloat16, device=DEV)
+    app = PagedPrefix(pool, torch.arange(64, 128, device=DEV))
+    with pytest.raises(ValueError, match="slots for"):
+        paged_attention(q, None, 0, q[:32], q[:32], append=app)
+    other = _pool(1, 2, 64, 4, seed=24)
+    slots, _ = _prefix(other, 64, seed=25)
+    with pytest.raises(ValueError, match="same pool"):
+        paged_attention(q, PagedPrefix(other, slots), 0, q, q, append=app)
+
+
 # ---- the tail computations either side of the pool (f2): encoder partial hit, DiT prefix prefill ----------------
 def _sdpa_ref(q, k, v, mask, scale):
     """fp32 attention with a boolean visibility mask [n_q, n_k], GQA by head repetition (the reference's

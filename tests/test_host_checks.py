@@ -186,3 +186,23 @@ def test_paged_attention_checks_arguments_before_any_cuda_call():
     with pytest.raises(ValueError, match="local"):
         call(n_loc=5)
     call(n_q=0)  # nothing to do: returns before touching the GPU
+
+    def call_append(**kw):
+        args = dict(q=16, qt=512, qh=256, n_q=4, hq=2, kp=16, vp=16, rows=128, hkv=2, bt=None, page=64, n_pre=0,
+                    kl=16, vl=16, lt=512, lh=256, n_loc=4, causal=0, scale=0.088, out=16, ot=512, oh=256, lse=None,
+                    app=16, err=16, stream=None)
+        args.update(kw)
+        _lib.call("qe_paged_attention_append", *args.values())
+
+    with pytest.raises(ValueError, match="null append table"):
+        call_append(app=None)
+    with pytest.raises(ValueError, match="error flag"):
+        call_append(err=None)
+    with pytest.raises(ValueError, match="nothing to append"):
+        call_append(n_loc=0, n_pre=10, bt=16)
+    with pytest.raises(ValueError, match="no queries"):
+        call_append(n_q=0)
+    with pytest.raises(ValueError, match="page_size"):
+        call_append(page=4)
+    with pytest.raises(ValueError, match="null pool"):
+        call_append(kp=None)
