@@ -16,7 +16,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from oracle.radix_ref import Allocator, RadixCache
+from oracle.radix_ref import Allocator, Clock, RadixCache
 
 
 @dataclass
@@ -48,7 +48,7 @@ def _key(vids) -> list:
 
 class RefPagedKVPool:
     def __init__(self, name, layers, heads, head_dim, budget_bytes, dtype, device="cpu", extra_dim=0, page_size=1,
-                 allocate=True):
+                 allocate=True, clock_resolution=1):
         elem = torch.empty((), dtype=dtype).element_size()
         per_token = layers * 2 * heads * head_dim * elem + extra_dim * elem
         self.name = name
@@ -60,7 +60,7 @@ class RefPagedKVPool:
         self.kv = torch.empty(layers, 2, rows, heads, head_dim, dtype=dtype, device=device) if allocate else None
         self.extra = torch.empty(rows, extra_dim, dtype=dtype, device=device) if (extra_dim and allocate) else None
         self.allocator = Allocator(self.capacity, page_size)
-        self.tree = RadixCache(self.allocator, page_size)
+        self.tree = RadixCache(self.allocator, page_size, Clock(clock_resolution))
         self.stats = PoolStats()
         self.lock = threading.RLock()
 

@@ -8,7 +8,10 @@ Follows the behaviour QwenEdit's PagedKVPool relies on (multi_turn/cache/paged.p
   insert split nodes; every node on a walk gets the walk's access time; ``evict`` heapifies leaves on
   last-access time and pops unlocked ones, pushing a parent that loses its last child; lock refs walk to
   the root moving tokens between evictable and protected.
-* time.monotonic() is a logical clock: one tick per walk and per node construction.
+* time.monotonic() is a logical clock: one tick per walk and per node construction. ``Clock(resolution=k)``
+  gives every k consecutive reads the same value instead: a wall clock too coarse to separate some reads, under
+  which leaves can tie on last-access time and the heap's layout decides between them (``evict`` then records
+  ``tie_seen``).
 
 Written in plain Python with dicts, lists and heapq so it reads like the original design; the product
 (libqeb200's C++ prefix index) is checked against it operation for operation.
@@ -23,11 +26,12 @@ import numpy as np
 
 
 class Clock:
-    def __init__(self):
-        self._t = itertools.count(1)
+    def __init__(self, resolution: int = 1):
+        self._t = itertools.count(0)
+        self.resolution = resolution
 
     def __call__(self) -> int:
-        return next(self._t)
+        return 1 + next(self._t) // self.resolution
 
 
 class TreeNode:
@@ -87,10 +91,11 @@ class Allocator:
 
 
 class RadixCache:
-    def __init__(self, allocator: Allocator, page_size: int = 1):
+    def __init__(self, allocator: Allocator, page_size: int = 1, clock: Clock | None = None):
         self.allocator = allocator
         self.page_size = page_size
-        self.clock = Clock()
+        self.clock = clock if clock is not None else Clock()
+        self.tie_seen = False  # an eviction chose between leaves of equal last-access time
         self.reset()
 
     # -- keys
@@ -215,7 +220,9 @@ class RadixCache:
         heapq.heapify(heap)
         evicted = 0
         while evicted < num_tokens and heap:
-            _, x = heapq.heappop(heap)
+            t, x = heapq.heappop(heap)
+            if heap and heap[0][0] == t:
+                self.tie_seen = True
             if x is self.root_node:
                 break
             if x.lock_ref > 0:

@@ -137,6 +137,52 @@ def test_random_sessions_match_oracle(page, seed):
     assert ours.usage()["protected"] == 0
 
 
+def _ref_pool(tokens, resolution):
+    return RefPagedKVPool("t", L, H, D, tokens * PER_TOKEN, torch.bfloat16, allocate=False,
+                          clock_resolution=resolution)
+
+
+def _lockstep(resolution, seed):
+    """The oracle with a logical and with a coarse clock on one workload: the step at which their results first
+    differ (None if never), and whether an eviction of the coarse one chose between tied leaves before that."""
+    rng = np.random.default_rng(100 + seed)
+    cap = int(rng.integers(150, 400))
+    logical, coarse = _ref_pool(cap, 1), _ref_pool(cap, resolution)
+    sessions = [list(rng.integers(1, 1 << 40, size=int(rng.integers(20, 90)))) for _ in range(6)]
+    for step in range(300):
+        s = int(rng.integers(len(sessions)))
+        if rng.random() < 0.4:
+            sessions[s] = sessions[s] + list(rng.integers(1, 1 << 40, size=int(rng.integers(1, 50))))
+        vids = np.asarray(sessions[s], np.int64)
+        a, b = fill(logical, vids), fill(coarse, vids)
+        same = a[0] == b[0] and (a[1] is None) == (b[1] is None) and (a[1] is None or np.array_equal(a[1], b[1]))
+        if not same or logical.usage() != coarse.usage():
+            return step, coarse.tree.tie_seen
+    assert not logical.tree.tie_seen  # the logical clock never ties two leaves
+    return None, coarse.tree.tie_seen
+
+
+@pytest.mark.parametrize("resolution", [2, 7, 50])
+@pytest.mark.parametrize("seed", range(4))
+def test_coarse_clock_diverges_only_through_ties(resolution, seed):
+    """SGLang stamps nodes with time.monotonic(); the oracle and the native index use a logical clock (every read a
+    new tick). Under a clock too coarse to separate reads, leaves can tie on last-access time and the eviction heap's
+    layout (heapq's sift order) picks the victim. The two agree at every operation until an eviction has had to
+    choose between tied leaves."""
+    step, tied = _lockstep(resolution, seed)
+    if step is not None:
+        assert tied, f"diverged at step {step} without a tied eviction"
+
+
+def test_coarse_clock_does_change_eviction_order():
+    """The divergence is real: with 7 or 50 reads per clock value every workload above diverges (after a tie),
+    so eviction order matches SGLang's only while its clock separates the reads, which the logical clock assumes."""
+    for resolution in (7, 50):
+        for seed in range(4):
+            step, tied = _lockstep(resolution, seed)
+            assert step is not None and tied
+
+
 def test_page_mode_truncates_and_frees_tail_pages():
     ours, ref = pools(64, page=16)
     for pool in (ours, ref):
