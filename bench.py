@@ -601,6 +601,26 @@ def attention_extras(pool, device):
         ms_ref = timed(gather_then_sdpa)
     except Exception:  # noqa: BLE001  (no cuDNN attention in this torch build)
         ms_ref = None
+    # the own K/V also stored into freshly allocated pool pages (a prefill tail, or the encoder's _store): in the
+    # attention launch itself (qe_paged_attention_append) against the attention then one write_layers launch
+    appended = None
+    tail_slots = pool.alloc(n)
+    if tail_slots is not None:
+        app = PagedPrefix(pool, tail_slots)
+        keys, values = [k_own] * L, [v_own] * L
+
+        def ours_append():
+            for layer in range(L):
+                paged_attention(q, prefix, layer, k_own, v_own, out=out, append=app)
+
+        def ours_then_write():
+            ours()
+            pool.write_layers(tail_slots, keys, values)
+
+        ms_app, ms_sep = timed(ours_append), timed(ours_then_write)
+        appended = {"tokens": n, "bytes_per_step": L * 2 * n * H * D * 2, "ms_per_step": round(ms_app, 3),
+                    "attention_then_write_layers_ms_per_step": round(ms_sep, 3),
+                    "append_cost_ms_per_step": round(ms_app - ms, 3)}
     if pool.device_errors():
         raise RuntimeError("the paged attention kernel reported an error")
     peaks = {}
@@ -612,7 +632,8 @@ def attention_extras(pool, device):
            "ms_per_step": round(ms, 3), "ms_per_layer": round(ms / L, 4), "TFLOP/s": round(tf, 1),
            "gather_then_cudnn_sdpa_ms_per_step": None if ms_ref is None else round(ms_ref, 3),
            "speedup_vs_gather_then_cudnn_sdpa": None if ms_ref is None else round(ms_ref / ms, 3),
-           "timing": "CUDA events around one step's 60 launches (inputs resident, 2.3 GB of prefix K/V per step > L2)"}
+           "timing": "CUDA events around one step's 60 launches (inputs resident, 2.3 GB of prefix K/V per step > L2)",
+           "fused_append": appended}
     if peaks.get("bf16_tflops_sustained"):
         res["frac_of_measured_bf16_sustained"] = round(tf / peaks["bf16_tflops_sustained"], 4)
         res["frac_of_measured_bf16_burst"] = round(tf / peaks["bf16_tflops"], 4)

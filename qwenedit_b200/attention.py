@@ -139,7 +139,8 @@ def paged_attention(q: torch.Tensor, prefix: PagedPrefix | None, layer: int = 0,
 
 
 def encoder_tail_attention(q: torch.Tensor, k_tail: torch.Tensor, v_tail: torch.Tensor, pool, indices: torch.Tensor,
-                           layer: int, scale: float, heads_buf: torch.Tensor | None = None) -> torch.Tensor:
+                           layer: int, scale: float, heads_buf: torch.Tensor | None = None,
+                           append: PagedPrefix | None = None) -> torch.Tensor:
     """One text-encoder layer's attention on a partial prefix hit (cache/encoder.py:173-190): the n tail queries
     attend over [the m cached prefix tokens; the n tail tokens], tail position i seeing the prefix and tail [0, i]
     (the reference's ``ones(n, m + n).tril(diagonal=m)`` mask), grouped-query heads (enable_gqa).
@@ -148,12 +149,18 @@ def encoder_tail_attention(q: torch.Tensor, k_tail: torch.Tensor, v_tail: torch.
     A page-mode pool (page size 8 to 128, or a multiple of 128) is read through its block table by the attention
     kernel itself. A token-granular pool (the reference's page size 1) is first gathered head-major with room for
     the tail (``pool.gather_heads``; pass the same `heads_buf` to every layer so it is gathered once), the tail
-    K/V written after the prefix, and the kernel attends over that buffer. Returns [n, Hq, 128] bf16."""
+    K/V written after the prefix, and the kernel attends over that buffer. Returns [n, Hq, 128] bf16.
+
+    `append` (page-mode pools): the slots allocated for the tail (``PagedPrefix(pool, pool.alloc(n))``); the same
+    launch stores this layer's tail K/V there (the K/V planes of encoder.py:131-138's _store; the hidden rows stay
+    ``pool.write_extra``)."""
     n = q.shape[0]
     m = int(indices.numel())
     if pool.page_size >= 8 and (128 % pool.page_size == 0 or pool.page_size % 128 == 0):
         return paged_attention(q, PagedPrefix(pool, indices) if m else None, layer, k_tail, v_tail, causal=True,
-                               scale=scale)
+                               scale=scale, append=append)
+    if append is not None:
+        raise ValueError("a fused append needs a page-mode pool (page size 8 to 128, or a multiple of 128)")
     if heads_buf is None:
         heads_buf = pool.gather_heads(indices, m + n)
     if heads_buf.shape[3] != m + n:
@@ -165,7 +172,8 @@ def encoder_tail_attention(q: torch.Tensor, k_tail: torch.Tensor, v_tail: torch.
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, prefix: PagedPrefix | None, layer: int,
-                      segments, start: int, scale: float | None = None) -> torch.Tensor:
+                      segments, start: int, scale: float | None = None,
+                      append: PagedPrefix | None = None) -> torch.Tensor:
     """The attention of the DiT's prefix prefill from position `start` (cache/prefill.py:32-72), one layer: the
     prefix positions [start, total) attend per segment (s, e, is_image) over keys [0, e), causally inside text
     segments (a text query at position p sees keys <= p), fully inside image segments. Keys [0, start) are the
@@ -173,15 +181,21 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, prefix:
 
     q, k, v [total - start, H, 128] bf16 for positions start .. total - 1; `segments` as the reference's layout
     (start and end positions over the whole prefix). Returns [total - start, H, 128]; one kernel launch per
-    segment that starts past `start`."""
+    segment that starts past `start`.
+
+    `append`: the pool slots of positions [start, total) (``PagedPrefix(pool, pool.alloc(total - start))``); the
+    last segment's launch, whose own keys are all of k / v, also stores this layer's K/V there (the
+    ``kv[l, :, m:]`` write of prefill.py:69-72 that the caller would otherwise append with ``pool.write``)."""
     n = q.shape[0]
     for s0, e, is_image in segments:  # as the reference checks before any layer runs
         if is_image and s0 < start < e:
             raise ValueError("cached prefix ends inside an image block")
     if start and (prefix is None or prefix.length != start):
         raise ValueError(f"the pooled prefix must hold the {start} positions before `start`")
+    if append is not None and (not segments or segments[-1][1] - start != n):
+        raise ValueError("a fused append needs the last segment to end at the last position given")
     out = torch.empty_like(q)
-    for s0, e, is_image in segments:
+    for i, (s0, e, is_image) in enumerate(segments):
         if e <= start:
             continue
         s = max(s0, start)
@@ -191,5 +205,5 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, prefix:
         if hi > n:
             raise ValueError(f"segment ends at {e}, past the {start + n} positions given")
         paged_attention(q[lo:hi], prefix if start else None, layer, k[:hi], v[:hi], causal=not is_image,
-                        scale=scale, out=out[lo:hi])
+                        scale=scale, out=out[lo:hi], append=append if i == len(segments) - 1 else None)
     return out

@@ -332,6 +332,70 @@ def test_prefill_attention_matches_the_segment_loop(start):
         _check(out[s - start:e - start], None, ref, None)
 
 
+def _free_slots(pool, used, n, seed):
+    """Slots for n tokens on whole pages of `pool` that hold none of the `used` slots (and not page 0)."""
+    P = pool.page_size
+    taken = set() if used is None else set((used.cpu().numpy() // P).tolist())
+    rng = np.random.default_rng(seed)
+    pages = np.array([p for p in rng.permutation(np.arange(1, pool.rows // P)).tolist() if p not in taken])
+    t = np.arange(n)
+    return torch.from_numpy(pages[: -(-n // P)][t // P] * P + t % P).to(DEV)
+
+
+def test_prefill_with_fused_append_stores_the_tail_of_every_layer():
+    """The prefix prefill from a cached head (prefill.py:32-72) with the tail's K/V appended by the attention
+    launches themselves: per layer the output equals the plain prefill's, and afterwards the pool holds, at the
+    cached slots then the tail slots, every layer's K/V of the whole prefix (what the reference's pool.write of
+    kv[:, :, m:] followed by insert leaves)."""
+    from qwenedit_b200.attention import prefill_attention
+
+    h, total, start, layers = 4, 900, 128, 2
+    segments = [(0, 128, False), (128, 640, True), (640, 900, False)]
+    pool = _pool(layers, h, 64, 20, seed=41)
+    slots, vals = _prefix(pool, start, seed=42)
+    tail = _free_slots(pool, slots, total - start, seed=43)
+    prefix, app = PagedPrefix(pool, slots), PagedPrefix(pool, tail)
+    g = torch.Generator(device=DEV).manual_seed(44)
+    kv_tail = torch.empty(layers, 2, total - start, h, D, dtype=torch.bfloat16, device=DEV)
+    for layer in range(layers):
+        q, k, v = (torch.randn(total - start, h, D, generator=g, device=DEV).bfloat16() for _ in range(3))
+        kv_tail[layer, 0], kv_tail[layer, 1] = k, v
+        want = prefill_attention(q, k, v, prefix, layer, segments, start)
+        got = prefill_attention(q, k, v, prefix, layer, segments, start, append=app)
+        assert torch.equal(got, want)
+    torch.cuda.synchronize()
+    assert pool.device_errors() == 0
+    whole = pool.kv[:, :, torch.cat([slots, tail])]
+    assert torch.equal(whole.view(torch.int16), torch.cat([vals, kv_tail], dim=2).view(torch.int16))
+    with pytest.raises(ValueError, match="last segment"):
+        prefill_attention(q[:-1], k[:-1], v[:-1], prefix, 0, segments, start, append=app)
+
+
+def test_encoder_tail_with_fused_append():
+    """encoder.py:131-138 after a partial hit: each layer's tail attention also stores the tail K/V into the slots
+    allocated for it (page-16 pool, grouped-query heads)."""
+    from qwenedit_b200.attention import encoder_tail_attention
+
+    layers, hq, hkv, m, n = 2, 28, 4, 320, 77
+    pool = _pool(layers, hkv, 16, -(-m // 16) + -(-n // 16) + 4, seed=51)
+    slots, vals = _prefix(pool, m, seed=52)
+    app = PagedPrefix(pool, _free_slots(pool, slots, n, seed=53))
+    g = torch.Generator(device=DEV).manual_seed(54)
+    scale = 128 ** -0.5
+    for layer in range(layers):
+        q = torch.randn(n, hq, D, generator=g, device=DEV).bfloat16()
+        k_t, v_t = (torch.randn(n, hkv, D, generator=g, device=DEV).bfloat16() for _ in range(2))
+        out = encoder_tail_attention(q, k_t, v_t, pool, slots, layer, scale, append=app)
+        mask = torch.ones(n, m + n, dtype=torch.bool, device=DEV).tril(diagonal=m)
+        ref = _sdpa_ref(q, torch.cat([vals[layer, 0], k_t]), torch.cat([vals[layer, 1], v_t]), mask, scale)
+        _check(out, None, ref, None)
+        assert torch.equal(pool.kv[layer, 0, app.indices], k_t) and torch.equal(pool.kv[layer, 1, app.indices], v_t)
+    assert pool.device_errors() == 0
+    tok = _pool(1, hkv, 1, 400, seed=55)
+    with pytest.raises(ValueError, match="page-mode"):
+        encoder_tail_attention(q, k_t, v_t, tok, torch.arange(1, 11, device=DEV), 0, scale, append=app)
+
+
 def test_prefill_attention_rejects_a_prefix_ending_inside_an_image():
     from qwenedit_b200.attention import prefill_attention
 
