@@ -51,6 +51,7 @@ constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the running max grows by more than this (log2 units)
+constexpr float kHalfSumBound = 16384.0f;  // 64 keys x 2^kRescaleLog2: a larger half-tile sum has a p above 2^8
 
 // shared memory, from a 1024-byte aligned base
 constexpr int kQOff = 0;
@@ -275,6 +276,11 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {  // two bf16 products, round to nearest
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
@@ -538,92 +544,216 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Tiles whose 128 keys are all visible to every row of the warp skip the per-key masks (warp-uniform).
       const bool masked = __any_sync(0xffffffffu, limit < kTile);
-      // pass 1: the row's max of the raw scores over the visible keys (S stays in tensor memory, read 32
-      // columns at a time; four independent three-input max chains), scaled once afterwards (scale > 0)
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      {
-        uint32_t buf[2][32];
-        tmem_ld32_async(s_col, buf[0]);
-        tmem_ld_wait(buf[0]);
+      // One pass over S once every row of the warp has a finite reference max m_use: p = 2^(s scale_log2 - m_use)
+      // with no max. A half tile (64 keys) whose p all stay <= 2^8 sums to <= 2^14, so a row whose max grew by more
+      // than 2^8 shows (at the latest once its growth makes a half sum pass 2^14; until then its p stay <= 2^14).
+      // Half A (keys 0-63) is written as P once no row's half sum passed the bound (else the two-pass path runs
+      // from the intact S); then half B. A row that passes in half B: its max over half B is read from S (those
+      // columns are not written yet); if it grew by more than 2^8, m_use moves up by a whole number k of octaves,
+      // the row's O, half-A P and row sum scale by 2^-k exactly, and half B is redone.
+      bool two_pass = true;
+      if (__all_sync(0xffffffffu, m_use != -INFINITY)) {
+        const f32x2 scale2 = pk2(p.scale_log2, p.scale_log2);
+        f32x2 nbase2 = pk2(-m_use, -m_use);
+        f32x2 la[2] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)}, lb[2] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
+        uint32_t buf[2][32], pw[32];
+        // 32 keys of chunk c: p = 2^(s scale_log2 - m_use) (hidden keys 0), row sums, P words 16 (c % 2) ..
+        auto chunk32 = [&](int c, const uint32_t(&b)[32], f32x2(&ls)[2]) {
+          float pv[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
-          float chunk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) chunk[i] = __uint_as_float(buf[c & 1][i]);
+          for (int i = 0; i < 16; ++i) {
+            const float2 x = up2(fma2(pk2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1])), scale2, nbase2));
+            pv[2 * i] = ex2(x.x);
+            pv[2 * i + 1] = ex2(x.y);
+          }
           if (masked) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : -INFINITY;
+            for (int i = 0; i < 32; ++i) pv[i] = 32 * c + i < limit ? pv[i] : 0.0f;
           }
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            m4[0] = max3(m4[0], chunk[i], chunk[i + 1]);
-            m4[1] = max3(m4[1], chunk[i + 2], chunk[i + 3]);
-            m4[2] = max3(m4[2], chunk[i + 4], chunk[i + 5]);
-            m4[3] = max3(m4[3], chunk[i + 6], chunk[i + 7]);
+          for (int i = 0; i < 16; ++i) {
+            ls[i & 1] = add2(ls[i & 1], pk2(pv[2 * i], pv[2 * i + 1]));
+            pw[16 * (c & 1) + i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
           }
-          if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
-        }
-      }
-      const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
-      // A row moves its reference max only when its max grew by more than 2^8 (also when m_use is still -inf and
-      // a key is visible); its O (earlier tiles' sums at the old max) is scaled down to match. The tensor-memory
-      // accesses are warp-collective, so a warp rescales together: rows that keep their max scale by 1.
-      const bool grow = mx > m_use + kRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        const float f = grow && m_use != -INFINITY ? ex2(m_use - mx) : 1.0f;
-        if (it > 0) {  // before the first P V, O holds nothing yet
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            uint32_t w[32];
-            tmem_ld32(o_col + 32 * c, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * f);
-            tmem_st32(o_col + 32 * c, w);
-          }
-        }
-        l *= f;
-        if (grow) m_use = mx;
-      }
-      // pass 2: p = 2^(s scale_log2 - base) (one FFMA and one ex2 per key) as bf16 pairs written over the S
-      // columns already read: chunk c's 32 scores (columns 32c ..) become P columns 16c .. 16c + 15. The row sum
-      // runs in eight independent partial sums.
-      const float nbase = m_use == -INFINITY ? 0.0f : -m_use;
-      const f32x2 scale2 = pk2(p.scale_log2, p.scale_log2), nbase2 = pk2(nbase, nbase);
-      f32x2 l4[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
-      {
-        uint32_t buf[2][32];
-        tmem_ld32_async(s_col, buf[0]);
-        tmem_ld_wait(buf[0]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
-          float chunk[32];
+        };
+        auto store_half = [&](uint32_t col) {  // P words 0-31 to columns col .. col + 31
           uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 x = up2(fma2(pk2(__uint_as_float(buf[c & 1][2 * i]), __uint_as_float(buf[c & 1][2 * i + 1])),
-                                      scale2, nbase2));
-            chunk[2 * i] = ex2(x.x);
-            chunk[2 * i + 1] = ex2(x.y);
-          }
-          if (masked) {
+          for (int i = 0; i < 16; ++i) w[i] = pw[i];
+          tmem_st16(col, w);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
-          }
+          for (int i = 0; i < 16; ++i) w[i] = pw[16 + i];
+          tmem_st16(col + 16, w);
+        };
+        auto half_sum = [&](const f32x2(&ls)[2]) {
+          const float2 a = up2(add2(ls[0], ls[1]));
+          return a.x + a.y;
+        };
+        tmem_ld32_async(s_col, buf[0]);
+        tmem_ld_wait(buf[0]);
+        tmem_ld32_async(s_col + 32, buf[1]);
+        chunk32(0, buf[0], la);
+        tmem_ld_wait(buf[1]);
+        tmem_ld32_async(s_col + 64, buf[0]);  // half B's first chunk arrives during chunk 1
+        chunk32(1, buf[1], la);
+        tmem_ld_wait(buf[0]);
+        const float suma = half_sum(la);
+        if (!__any_sync(0xffffffffu, suma > kHalfSumBound)) {
+          two_pass = false;
+          store_half(s_col);
+          auto half_b = [&]() {  // buf[0] holds chunk 2
+            tmem_ld32_async(s_col + 96, buf[1]);
+            chunk32(2, buf[0], lb);
+            tmem_ld_wait(buf[1]);
+            chunk32(3, buf[1], lb);
+          };
+          half_b();
+          float lsum = l + suma, sumb = half_sum(lb);
+          if (__any_sync(0xffffffffu, sumb > kHalfSumBound)) {
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            tmem_ld32_async(s_col + 96, buf[1]);
+            tmem_ld32_async(s_col + 64, buf[0]);
+            tmem_ld_wait(buf[1]);
+            tmem_ld_wait(buf[0]);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            l4[i & 3] = add2(l4[i & 3], pk2(chunk[2 * i], chunk[2 * i + 1]));
-            w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  v[j] = 64 + 32 * h + i + j < limit ? __uint_as_float(buf[h][i + j]) : -INFINITY;
+                m4[0] = max3(m4[0], v[0], v[1]);
+                m4[1] = max3(m4[1], v[2], v[3]);
+                m4[2] = max3(m4[2], v[4], v[5]);
+                m4[3] = max3(m4[3], v[6], v[7]);
+              }
+            }
+            const float mb = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
+            const bool grow = mb > m_use + kRescaleLog2;
+            if (__any_sync(0xffffffffu, grow)) {
+              const int k = grow ? int(ceilf(fminf(mb - m_use, 1000.0f))) : 0;
+              const uint32_t fb = k <= 126 ? uint32_t(127 - k) << 23 : 0u;  // 2^-k (0 below the normal range)
+              const float f = __uint_as_float(fb);
+              const uint32_t f2 = (fb >> 16) | (fb & 0xffff0000u);  // the same as a bf16 pair
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float o[32];
+                uint32_t w[32];
+                tmem_ld32(o_col + 32 * c, o);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * f);
+                tmem_st32(o_col + 32 * c, w);
+              }
+              tmem_wait_st();  // half A's P is in tensor memory before it is read back
+              {
+                float pa[32];
+                uint32_t w[32];
+                tmem_ld32(s_col, pa);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) w[i] = bmul2(__float_as_uint(pa[i]), f2);
+                tmem_st32(s_col, w);
+              }
+              lsum *= f;
+              m_use += float(k);
+              nbase2 = pk2(-m_use, -m_use);
+              lb[0] = lb[1] = pk2(0.0f, 0.0f);
+              half_b();  // buf[0] still holds chunk 2
+              sumb = half_sum(lb);
+            }
           }
-          tmem_st16(s_col + 16 * c, w);  // columns 16c .. 16c + 15: already read, not those in flight
-          if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
+          store_half(s_col + 32);
+          l = lsum + sumb;
         }
       }
-      {
-        const float2 a = up2(add2(add2(l4[0], l4[1]), add2(l4[2], l4[3])));
-        l += a.x + a.y;
+      if (two_pass) {
+        // pass 1: the row's max of the raw scores over the visible keys (S stays in tensor memory, read 32
+        // columns at a time; four independent three-input max chains), scaled once afterwards (scale > 0)
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        {
+          uint32_t buf[2][32];
+          tmem_ld32_async(s_col, buf[0]);
+          tmem_ld_wait(buf[0]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
+            float chunk[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) chunk[i] = __uint_as_float(buf[c & 1][i]);
+            if (masked) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              m4[0] = max3(m4[0], chunk[i], chunk[i + 1]);
+              m4[1] = max3(m4[1], chunk[i + 2], chunk[i + 3]);
+              m4[2] = max3(m4[2], chunk[i + 4], chunk[i + 5]);
+              m4[3] = max3(m4[3], chunk[i + 6], chunk[i + 7]);
+            }
+            if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
+          }
+        }
+        const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
+        // A row moves its reference max only when its max grew by more than 2^8 (also when m_use is still -inf and
+        // a key is visible); its O (earlier tiles' sums at the old max) is scaled down to match. The tensor-memory
+        // accesses are warp-collective, so a warp rescales together: rows that keep their max scale by 1.
+        const bool grow = mx > m_use + kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float f = grow && m_use != -INFINITY ? ex2(m_use - mx) : 1.0f;
+          if (it > 0) {  // before the first P V, O holds nothing yet
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float o[32];
+              uint32_t w[32];
+              tmem_ld32(o_col + 32 * c, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * f);
+              tmem_st32(o_col + 32 * c, w);
+            }
+          }
+          l *= f;
+          if (grow) m_use = mx;
+        }
+        // pass 2: p = 2^(s scale_log2 - base) (one FFMA and one ex2 per key) as bf16 pairs written over the S
+        // columns already read: chunk c's 32 scores (columns 32c ..) become P columns 16c .. 16c + 15. The row sum
+        // runs in eight independent partial sums.
+        const float nbase = m_use == -INFINITY ? 0.0f : -m_use;
+        const f32x2 scale2 = pk2(p.scale_log2, p.scale_log2), nbase2 = pk2(nbase, nbase);
+        f32x2 l4[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
+        {
+          uint32_t buf[2][32];
+          tmem_ld32_async(s_col, buf[0]);
+          tmem_ld_wait(buf[0]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c + 1 < 4) tmem_ld32_async(s_col + 32 * (c + 1), buf[(c + 1) & 1]);  // next chunk in flight
+            float chunk[32];
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float2 x = up2(fma2(pk2(__uint_as_float(buf[c & 1][2 * i]), __uint_as_float(buf[c & 1][2 * i + 1])),
+                                        scale2, nbase2));
+              chunk[2 * i] = ex2(x.x);
+              chunk[2 * i + 1] = ex2(x.y);
+            }
+            if (masked) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) chunk[i] = 32 * c + i < limit ? chunk[i] : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              l4[i & 3] = add2(l4[i & 3], pk2(chunk[2 * i], chunk[2 * i + 1]));
+              w[i] = pack_bf16(chunk[2 * i], chunk[2 * i + 1]);
+            }
+            tmem_st16(s_col + 16 * c, w);  // columns 16c .. 16c + 15: already read, not those in flight
+            if (c + 1 < 4) tmem_ld_wait(buf[(c + 1) & 1]);
+          }
+        }
+        {
+          const float2 a = up2(add2(add2(l4[0], l4[1]), add2(l4[2], l4[3])));
+          l += a.x + a.y;
+        }
       }
       tmem_wait_st();
       tc_fence_before();

@@ -133,6 +133,44 @@ def test_growing_maximum_rescales_the_output():
     _check(out, lse, ref_out, ref_lse)
 
 
+def test_max_growth_in_each_half_of_a_tile():
+    """Scores built so that the row max jumps by about 20 octaves inside the second half of key tile 1 and again
+    inside the first half of tile 2, then stays low in tile 3: every row takes the one-pass path with a half-B
+    rescale (O, half-A P and row sum scaled by a power of two, half B redone), the two-pass path from a half-A
+    jump, and the plain one-pass path."""
+    n_q, n_k, h = 128, 512, 2
+    scale = 1 / math.sqrt(D)
+    step = 20.0 / (scale * math.log2(math.e))  # a score step of 20 octaves after scaling
+    g = torch.Generator(device=DEV).manual_seed(61)
+    q = torch.zeros(n_q, h, D, device=DEV)
+    q[:, :, 0] = 1.0
+    q[:, :, 1:] = torch.randn(n_q, h, D - 1, generator=g, device=DEV) * 0.1
+    c = torch.zeros(n_k, device=DEV)
+    c[128 + 64: 256] = step        # tile 1, half B
+    c[256: 256 + 32] = 2 * step    # tile 2, half A
+    c[256 + 32: 384] = step
+    k = torch.randn(n_k, h, D, generator=g, device=DEV) * 0.1
+    k[:, :, 0] = c[:, None] + torch.randn(n_k, h, generator=g, device=DEV)
+    v = torch.randn(n_k, h, D, generator=g, device=DEV)
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    out, lse = paged_attention(q, None, 0, k, v, scale=scale, return_lse=True)
+    ref_out, ref_lse = _reference(q, k, v, scale, False, n_k)
+    _check(out, lse, ref_out, ref_lse)
+    # without the last two tiles, the half-B rescale decides the output alone
+    out2, lse2 = paged_attention(q, None, 0, k[:256], v[:256], scale=scale, return_lse=True)
+    ref2, ref_lse2 = _reference(q, k[:256], v[:256], scale, False, 256)
+    _check(out2, lse2, ref2, ref_lse2)
+    # growth a half-tile sum does not show: one key 12 octaves up in tile 1 (its p stays below 2^14), then a
+    # whole tile there
+    k3 = k.clone()
+    k3[:, :, 0] = torch.randn(n_k, h, generator=g, device=DEV).bfloat16()
+    k3[128 + 5, :, 0] = 0.6 * step
+    k3[256:384, :, 0] = 0.6 * step
+    out3, lse3 = paged_attention(q, None, 0, k3, v, scale=scale, return_lse=True)
+    ref3, ref_lse3 = _reference(q, k3, v, scale, False, n_k)
+    _check(out3, lse3, ref3, ref_lse3)
+
+
 def test_page_outside_the_pool_reads_zeros_and_is_reported():
     page, h, n_prefix = 64, 2, 256
     pool = _pool(1, h, page, 6, seed=5)
