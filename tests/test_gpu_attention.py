@@ -228,6 +228,7 @@ APPEND_CASES = [  # (page, heads_q, heads_kv, n_q, n_prefix, n_local, causal, la
     (16, 2, 2, 257, 0, 257, False, 1, 0),      # first turn (no prefix), pages shorter than a key tile
     (256, 2, 1, 512, 512, 700, False, 2, 0),   # pages of two key tiles, more own keys than queries
     (128, 2, 2, 1024, 4096, 1024, False, 1, 0),  # whole pages
+    (8, 4, 1, 200, 64, 200, True, 1, 0),       # the smallest page: 16 pages per key tile, 4 query heads per K/V head
 ]
 
 
@@ -380,19 +381,23 @@ def _free_slots(pool, used, n, seed):
     return torch.from_numpy(pages[: -(-n // P)][t // P] * P + t % P).to(DEV)
 
 
-def test_prefill_with_fused_append_stores_the_tail_of_every_layer():
+@pytest.mark.parametrize("start", [0, 128])
+def test_prefill_with_fused_append_stores_the_tail_of_every_layer(start):
     """The prefix prefill from a cached head (prefill.py:32-72) with the tail's K/V appended by the attention
     launches themselves: per layer the output equals the plain prefill's, and afterwards the pool holds, at the
     cached slots then the tail slots, every layer's K/V of the whole prefix (what the reference's pool.write of
-    kv[:, :, m:] followed by insert leaves)."""
+    kv[:, :, m:] followed by insert leaves). start 0: a miss, the whole prefix computed and stored."""
     from qwenedit_b200.attention import prefill_attention
 
-    h, total, start, layers = 4, 900, 128, 2
+    h, total, layers = 4, 900, 2
     segments = [(0, 128, False), (128, 640, True), (640, 900, False)]
     pool = _pool(layers, h, 64, 20, seed=41)
-    slots, vals = _prefix(pool, start, seed=42)
+    if start:
+        slots, vals = _prefix(pool, start, seed=42)
+    else:
+        slots, vals = None, torch.empty(layers, 2, 0, h, D, dtype=torch.bfloat16, device=DEV)
     tail = _free_slots(pool, slots, total - start, seed=43)
-    prefix, app = PagedPrefix(pool, slots), PagedPrefix(pool, tail)
+    prefix, app = (PagedPrefix(pool, slots) if start else None), PagedPrefix(pool, tail)
     g = torch.Generator(device=DEV).manual_seed(44)
     kv_tail = torch.empty(layers, 2, total - start, h, D, dtype=torch.bfloat16, device=DEV)
     for layer in range(layers):
@@ -403,7 +408,7 @@ def test_prefill_with_fused_append_stores_the_tail_of_every_layer():
         assert torch.equal(got, want)
     torch.cuda.synchronize()
     assert pool.device_errors() == 0
-    whole = pool.kv[:, :, torch.cat([slots, tail])]
+    whole = pool.kv[:, :, tail if slots is None else torch.cat([slots, tail])]
     assert torch.equal(whole.view(torch.int16), torch.cat([vals, kv_tail], dim=2).view(torch.int16))
     with pytest.raises(ValueError, match="last segment"):
         prefill_attention(q[:-1], k[:-1], v[:-1], prefix, 0, segments, start, append=app)
