@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kVFull + s), 1);
       mbar_init(bar(kVEmpty + s), 1);
       mbar_init(bar(kSFull + s), 1);
-      mbar_init(bar(kPReady + s), kTile);
+      mbar_init(bar(kPReady + s), 4);  // one arrival per softmax warp of the tile
     }
     mbar_init(bar(kOFinal), 1);
     mbar_init(bar(kDrain), 1);
@@ -757,7 +757,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kPReady + t));
+      __syncwarp();  // every lane's P is written before the warp's one arrival
+      if (lane == 0) mbar_arrive(bar(kPReady + t));
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(kOFinal), 0, abort, p.err));
     if (ok) {
