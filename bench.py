@@ -482,6 +482,37 @@ def encoder_extras(device, peak):
 
     tail_ms = _time_graph([ours])
     tail_ref_ms = _time_graph([reference_ops])
+    # the partial hit's attention (encoder.py:173-190): 28 query heads over [prefix; tail] with the reference's
+    # tril(diagonal=m) mask, every layer: the paged kernel over the head-major gather (token-granular pool) against
+    # the reference's gather + per-layer transpose / cat + masked GQA SDPA
+    import torch.nn.functional as F
+
+    from qwenedit_b200.attention import encoder_tail_attention
+
+    hq, scale = 28, hd ** -0.5
+    q_t = torch.randn(tail, hq, hd, device=device).bfloat16()
+    kv_t = torch.randn(2, tail, kvh, hd, device=device).bfloat16()
+    heads_out = torch.empty(tail, hq, hd, dtype=torch.bfloat16, device=device)
+    mask = torch.ones(tail, n + tail, dtype=torch.bool, device=device).tril(diagonal=n)
+
+    def ours_attention():
+        buf = pool.gather_heads(slots, n + tail)
+        for layer in range(layers):
+            heads_out.copy_(encoder_tail_attention(q_t, kv_t[0], kv_t[1], pool, slots, layer, scale, heads_buf=buf))
+
+    def reference_attention():
+        cached = pool.gather(slots)
+        for layer in range(layers):
+            k = torch.cat([cached[layer, 0].transpose(0, 1)[None], kv_t[0].transpose(0, 1)[None]], dim=2)
+            v = torch.cat([cached[layer, 1].transpose(0, 1)[None], kv_t[1].transpose(0, 1)[None]], dim=2)
+            F.scaled_dot_product_attention(q_t.transpose(0, 1)[None], k, v, attn_mask=mask, scale=scale,
+                                           enable_gqa=True)
+
+    att_ms = _time_graph([ours_attention])
+    try:
+        att_ref_ms = _time_graph([reference_attention])
+    except Exception:  # noqa: BLE001  (a torch build whose masked GQA SDPA does not capture)
+        att_ref_ms = None
     # steady state: 8 prompts' gathers back to back from one CUDA graph, each prompt's own scattered slots and
     # output (0.94 GB of K/V in total, > L2), so every launch reads HBM and no launch latency is in the time
     prompts = [pool.alloc(n) for _ in range(8)]
@@ -501,7 +532,12 @@ def encoder_extras(device, peak):
                              "timing": "8 prompts back to back from one CUDA graph, per-launch mean"},
             "partial_hit_prefix_ms": {"gather_heads_plus_tail_writes": round(tail_ms, 4),
                                       "gather_then_per_layer_transpose_cat": round(tail_ref_ms, 4),
-                                      "prefix_tokens": n, "tail_tokens": tail, "timing": "CUDA graph, device time"}}
+                                      "prefix_tokens": n, "tail_tokens": tail, "timing": "CUDA graph, device time"},
+            "partial_hit_attention_ms": {"gather_heads_then_paged_attention": round(att_ms, 4),
+                                         "gather_cat_masked_gqa_sdpa": None if att_ref_ms is None else
+                                         round(att_ref_ms, 4),
+                                         "layers": layers, "query_heads": hq, "kv_heads": kvh, "prefix_tokens": n,
+                                         "tail_tokens": tail, "timing": "CUDA graph, device time, all layers"}}
 
 
 def latent_extras(device):
