@@ -102,7 +102,8 @@ int qe_append_slots_ptrs(qe_planes pool, int64_t pool_rows, const void *const *s
  * up front), or code paths that must not allocate. No counterpart in the reference.
  * Limits: n_planes <= 1024 (an 8 KiB table per GPU that loads the library, held until exit); larger calls fail
  * with QE_ERR_INVALID before any work. The first call on each device looks the table up with
- * cudaGetSymbolAddress. Every call rewrites the table's
+ * cudaGetSymbolAddress (a set-up step, done once per device with that device current), so make that first call
+ * before any stream capture. Every call rewrites the table's
  * first n_planes entries on `stream` and the kernel reads them from there: calls whose work can overlap on the
  * GPU (different streams) race on the shared table; issue them on one stream. Host threads calling on one stream
  * are serialised by a per-device lock held from the table write through the launch, so their table writes and
