@@ -696,10 +696,15 @@ def _time_kernel(fn, flush, iters=20):
     return statistics.median(times)
 
 
-def _time_graph(calls, reps: int = 5) -> float:
+def _time_graph(calls, reps: int = 5, min_launches: int = 1) -> float:
     """ms per call of `calls` launched back to back from one CUDA graph (no host time between launches); the
     calls read distinct input copies whose total exceeds the L2, so each reads its input from HBM. Median of
-    `reps` replays."""
+    `reps` replays. With fewer calls than `min_launches` the list is cycled up to that many launches (consecutive
+    launches still read different copies): the graph's own start-up latency, which the events around a replay
+    include, is then shared by enough launches not to inflate the per-launch time (with two launches per graph
+    it added about 2 us to each 50 us launch on a B200)."""
+    if len(calls) < min_launches:
+        calls = [calls[i % len(calls)] for i in range(min_launches)]
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -724,6 +729,9 @@ def _time_graph(calls, reps: int = 5) -> float:
     return statistics.median(times)
 
 
+GRAPH_LAUNCHES = 24  # launches per timing graph for the NVFP4 extras
+
+
 def _copies(nbytes_each: int) -> int:
     return max(2, -(-(320 << 20) // nbytes_each))  # > 2.5x the 126 MB L2 in total
 
@@ -731,7 +739,8 @@ def _copies(nbytes_each: int) -> int:
 def nvfp4_extras(device, peak):
     """NVFP4 producers at the benchmark shapes (norm T = 4096 / 16384 / 32768 at K = 3072, SiLU T = 4096 / 16384 /
     32768 at K = 12288). `ms`: back-to-back launches from a CUDA graph, each on its own input copy (HBM-resident);
-    `ms_single_launch`: one launch between CUDA events after an L2 flush (includes the launch latency).
+    `ms_single_launch`: one launch between CUDA events after an L2 flush (includes the launch latency). Graphs
+    hold at least GRAPH_LAUNCHES launches (the input copies cycled), as the kernels run inside a DiT forward.
     `nvfp4_vs_triton`: the reference's own Triton kernels (fibo/fp4.py:64-116, from the offline install under
     baseline/_ref) timed the same way on the same inputs, next to ours on identical work (no adaLN shift, which
     the reference kernel does not have), with the encodings compared."""
@@ -750,7 +759,7 @@ def nvfp4_extras(device, peak):
     out, vs = {}, {}
 
     def record(name, nbytes, calls, single):
-        ms = _time_graph(calls)
+        ms = _time_graph(calls, min_launches=GRAPH_LAUNCHES)
         ms1 = _time_kernel(single, flush)
         out[name] = {"ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
                      "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peak, 4), "ms_single_launch": round(ms1, 4)}
@@ -758,7 +767,8 @@ def nvfp4_extras(device, peak):
     def versus(name, nbytes, ours_calls, ref_calls, compare):
         if ref is None:
             return
-        ours_ms, ref_ms = _time_graph(ours_calls), _time_graph(ref_calls)
+        ours_ms = _time_graph(ours_calls, min_launches=GRAPH_LAUNCHES)
+        ref_ms = _time_graph(ref_calls, min_launches=GRAPH_LAUNCHES)
         vs[name] = {"ours_ms": round(ours_ms, 4), "triton_ms": round(ref_ms, 4),
                     "ours_GB/s": round(nbytes / ours_ms / 1e6, 1), "triton_GB/s": round(nbytes / ref_ms / 1e6, 1),
                     "speedup": round(ref_ms / ours_ms, 3), "parity": compare()}
