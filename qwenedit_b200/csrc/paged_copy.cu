@@ -259,18 +259,21 @@ struct HeadsParams {
   int64_t pool_rows, n_tokens, row_bytes, head_bytes, out_head_stride, out_token_stride;
   const int64_t *slots;
   int32_t n_planes, rows_per_pass;
-  int32_t head_shift;  // log2(head_bytes / 16) when that is a power of two, else -1
+  int32_t head_shift;  // log2(head_bytes / vector bytes) when that is a power of two, else -1
   int32_t *err;
 };
 
-// Loads of a pass first (16 vectors per lane, a validity bitmask), then a second walk over the same vectors
+// Loads of a pass first (kUnroll vectors per lane, a validity bitmask), then a second walk over the same vectors
 // for their head-major destinations, so no destination pointer is kept live across the loads; the head of a
-// vector is a shift when the head size is a power of two (head_shift >= 0).
+// vector is a shift when the head size is a power of two (head_shift >= 0). V = int4 with 16 vectors per lane,
+// or Vec32 (256-bit loads and stores, every address 32-byte aligned) with 8: the same bytes in flight with half
+// the memory instructions.
+template <typename V, int kUnroll>
 __global__ void __launch_bounds__(kThreads, 2) gather_heads_kernel(HeadsParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * kThreads) >> 5;
-  const int vpr = int(p.row_bytes / 16), vph = int(p.head_bytes / 16);
+  const int vpr = int(p.row_bytes / int64_t(sizeof(V))), vph = int(p.head_bytes / int64_t(sizeof(V)));
   const int R = p.rows_per_pass;
   const int64_t blocks_per_plane = (p.n_tokens + R - 1) / R;
   const int64_t items = int64_t(p.n_planes) * blocks_per_plane;
@@ -287,16 +290,16 @@ __global__ void __launch_bounds__(kThreads, 2) gather_heads_kernel(HeadsParams p
     }
     const char *pool_plane = p.pool.plane(plane);
     char *out_plane = p.out.plane(plane) + t0 * p.out_token_stride;
-    for (int base = 0; base < R * vpr; base += 32 * kRowsUnroll) {
-      int4 buf[kRowsUnroll];
+    for (int base = 0; base < R * vpr; base += 32 * kUnroll) {
+      V buf[kUnroll];
       uint32_t valid = 0u;
       int ri = (base + lane) / vpr, vin = (base + lane) - ri * vpr;
 #pragma unroll
-      for (int k = 0; k < kRowsUnroll; ++k) {
+      for (int k = 0; k < kUnroll; ++k) {
         const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
         if (ri < R && slot >= 0) {
           valid |= 1u << k;
-          buf[k] = ld_stream(reinterpret_cast<const int4 *>(pool_plane + slot * p.row_bytes) + vin);
+          buf[k] = load_v<V>(reinterpret_cast<const V *>(pool_plane + slot * p.row_bytes) + vin);
         }
         vin += 32;
         while (vin >= vpr) {
@@ -307,12 +310,19 @@ __global__ void __launch_bounds__(kThreads, 2) gather_heads_kernel(HeadsParams p
       ri = (base + lane) / vpr;
       vin = (base + lane) - ri * vpr;
 #pragma unroll
-      for (int k = 0; k < kRowsUnroll; ++k) {
+      for (int k = 0; k < kUnroll; ++k) {
         if (valid & (1u << k)) {
           const int h = p.head_shift >= 0 ? vin >> p.head_shift : vin / vph;
           const int w = vin - h * vph;
-          *(reinterpret_cast<int4 *>(out_plane + h * p.out_head_stride + int64_t(ri) * p.out_token_stride) + w) =
-              buf[k];
+          V *dst = reinterpret_cast<V *>(out_plane + h * p.out_head_stride + int64_t(ri) * p.out_token_stride) + w;
+          if constexpr (sizeof(V) == 32) {  // a plain (not streaming) 256-bit store: the buffer is read next
+            const Vec32 &v = reinterpret_cast<const Vec32 &>(buf[k]);
+            asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(v.w[0]), "r"(v.w[1]),
+                         "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+                         : "memory");
+          } else {
+            *dst = buf[k];
+          }
         }
         vin += 32;
         while (vin >= vpr) {
@@ -806,16 +816,27 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
   p.out_token_stride = out_token_stride;
   p.slots = slots;
   p.n_planes = n_planes;
-  p.rows_per_pass = int32_t(std::max<int64_t>(1, std::min<int64_t>(32 * qe::kRowsUnroll / (row_bytes / 16), 32)));
+  // 256-bit vectors when every address of the copy is 32-byte aligned (the encoder's 1 KiB rows of 256-byte heads
+  // into a buffer from the caching allocator), unless the copy mode asks for 16-byte vectors
+  const bool wide = qe::g_copy_mode.load(std::memory_order_relaxed) != 4 && row_bytes % 32 == 0 &&
+                    head_bytes % 32 == 0 && out_head_stride % 32 == 0 && out_token_stride % 32 == 0 &&
+                    qe::planes_aligned(pool, 32) && qe::planes_aligned(out, 32);
+  const int64_t vec = wide ? 32 : 16, unroll = wide ? 8 : qe::kRowsUnroll;
+  p.rows_per_pass = int32_t(std::max<int64_t>(1, std::min<int64_t>(32 * unroll / (row_bytes / vec), 32)));
   p.head_shift = -1;
   for (int sh = 0; sh < 31; ++sh)
-    if ((int64_t(1) << sh) == head_bytes / 16) p.head_shift = sh;
+    if ((int64_t(1) << sh) == head_bytes / vec) p.head_shift = sh;
   p.err = err_flag;
   const int64_t items = int64_t(n_planes) * ((n_tokens + p.rows_per_pass - 1) / p.rows_per_pass);
   const int64_t warps_per_block = qe::kThreads / 32;
   int64_t blocks = std::min<int64_t>((items + warps_per_block - 1) / warps_per_block, int64_t(qe::sm_count()) * 2);
   blocks = std::max<int64_t>(blocks, 1);
-  qe::gather_heads_kernel<<<dim3(unsigned(blocks)), dim3(qe::kThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
+  if (wide)
+    qe::gather_heads_kernel<qe::Vec32, 8>
+        <<<dim3(unsigned(blocks)), dim3(qe::kThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
+  else
+    qe::gather_heads_kernel<int4, qe::kRowsUnroll>
+        <<<dim3(unsigned(blocks)), dim3(qe::kThreads), 0, static_cast<cudaStream_t>(stream)>>>(p);
   int s = qe::cuda_status(cudaGetLastError(), "qe_gather_slots_heads launch");
   return s ? s : qe::ok();
 }
