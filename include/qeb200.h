@@ -119,8 +119,10 @@ int qe_append_slots_ptrs_noalloc(qe_planes pool, int64_t pool_rows, const void *
  * which gathers [L, 2, m, H, D] and then builds [1, H, m + n, D] per layer by transpose + cat): for every plane
  * p, token t < n_tokens and head h, the head_bytes of head h of pool row slots[t] go to
  *   out.plane(p) + h * out_head_stride + t * out_token_stride.
- * row_bytes = heads * head_bytes; everything 16-byte aligned. Slots outside [0, pool_rows) are skipped and set
- * *err_flag. No counterpart as such in the reference (it is index_select + transpose + cat). */
+ * row_bytes = heads * head_bytes; everything 16-byte aligned. When everything is also 32-byte aligned (and the
+ * copy mode is not 4) the copy moves 256-bit vectors, else 16-byte ones; the result is the same. Slots outside
+ * [0, pool_rows) are skipped and set *err_flag. No counterpart as such in the reference (it is index_select +
+ * transpose + cat). */
 int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int32_t n_planes, int64_t row_bytes,
                           int64_t head_bytes, int64_t out_head_stride, int64_t out_token_stride, const int64_t *slots,
                           int64_t n_tokens, int32_t *err_flag, void *stream);
@@ -129,8 +131,8 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
  * most 1 KiB are moved several per warp pass; rows above 1 KiB on 32-byte aligned planes move in 256-bit
  * vectors, else 16-byte ones), 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned
  * rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per warp pass whatever the row
- * size, 4 = the warp kernel with 16-byte vectors only. No counterpart in the reference; for measurement and
- * tuning. */
+ * size, 4 = the warp kernel with 16-byte vectors only (also for qe_gather_slots_heads). No counterpart in the
+ * reference; for measurement and tuning. */
 int qe_set_paged_copy_mode(int32_t mode);
 
 /* ---- fused NVFP4 activation quantisers (device) ---------------------------------------------
