@@ -256,6 +256,13 @@ int qe_paged_attention_append(const void *q, int64_t q_token_stride, int64_t q_h
                               int64_t out_token_stride, int64_t out_head_stride, float *lse,
                               const int32_t *append_table, int32_t *err_flag, void *stream);
 
+/* Query tiles (of 128 queries) per CTA of qe_paged_attention / qe_paged_attention_append (process-wide): 0 = by
+ * grid size (default: one tile per CTA when ceil(n_q / 128) x heads_q CTAs fit on the GPU's SMs at once, which
+ * doubles the CTAs of small launches such as the encoder tail's; else two, whose softmax phases hide each
+ * other's), 1 or 2 forced. Results are the same within the kernel's rounding. No counterpart in the reference;
+ * for measurement and tests. */
+int qe_set_attention_q_tiles(int32_t q_tiles);
+
 /* ---- head-sharded pools across the GPUs of one node ------------------------------------------
  *
  * No counterpart in the reference, which keeps a prefix on one GPU and disables the pool under tensor or

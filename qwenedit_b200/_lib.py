@@ -62,6 +62,7 @@ SIGNATURES: dict[str, list] = {
     "qe_append_scatter": [c_void_p, c_int32, Planes, c_int64, Planes, c_int32, c_int64, c_void_p, c_int64,
                           c_void_p, c_void_p],
     "qe_set_norm_table_mode": [c_int32],
+    "qe_set_attention_q_tiles": [c_int32],
     "qe_set_silu_table_mode": [c_int32],
     "qe_set_silu_pipeline": [c_int32],
     "qe_set_nvfp4_numerics": [c_int32],

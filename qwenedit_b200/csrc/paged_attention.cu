@@ -9,7 +9,9 @@
 // The same kernel covers the text encoder's partial hit (cache/encoder.py:173-190): grouped-query heads and a
 // bottom-right causal mask on the step's own (tail) keys.
 //
-// Per CTA: two 128-query tiles of one query head (M = 256), head_dim 128, bf16 in, fp32 accumulation, bf16 out.
+// Per CTA: two 128-query tiles of one query head (M = 256), head_dim 128, bf16 in, fp32 accumulation, bf16 out;
+// or one tile (q_tiles = 1, warps 4-7 idle) when one-tile CTAs fit on the SMs in one wave, so that a small grid
+// (the encoder tail's 28 heads x 256 queries) runs twice the CTAs, each with half the work.
 //   warp 8       TMA producer: the Q tiles once, then per 128-key tile the K tile and the V tile into a
 //                two-stage ring each (pool pages: 4-D tensor maps [D, H, row-in-page, page] of the K or V plane of
 //                the layer; the step's own keys: 3-D maps [D, H, token])
@@ -42,7 +44,7 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kTile = 128;                       // queries per Q tile, keys per K/V tile
-constexpr int kQTiles = 2;                       // Q tiles per CTA
+constexpr int kQTiles = 2;                       // Q tiles per CTA at most (AttnParams::q_tiles: 1 or 2)
 constexpr int kTileBytes = kTile * kHeadDim * 2;  // 32 KiB: one Q, K or V tile
 constexpr int kHalfBytes = kTileBytes / 2;        // 16 KiB: 128 rows x 64 dims, one 128-byte swizzle span per row
 constexpr int kThreads = 320;                     // 8 softmax warps, the producer, the MMA warp
@@ -72,6 +74,7 @@ struct AttnParams {
   const int32_t *append_table;
   int32_t append_last_page, append_tail_rows;
   int32_t n_q, n_local, heads_q, group, causal;
+  int32_t q_tiles;  // Q tiles per CTA: 2, or 1 for grids that fit one wave of one-tile CTAs
   float scale_log2;
   __nv_bfloat16 *out;
   int64_t out_token_stride, out_head_stride;  // elements
@@ -293,7 +296,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ int own_key_tiles(const AttnParams &p, int x) {
   if (p.n_local <= 0) return 0;
   int last_key = p.n_local - 1;
-  if (p.causal) last_key = min(last_key, min((x + 1) * kQTiles * kTile, p.n_q) - 1 + p.n_local - p.n_q);
+  if (p.causal) last_key = min(last_key, min((x + 1) * p.q_tiles * kTile, p.n_q) - 1 + p.n_local - p.n_q);
   return last_key >= 0 ? last_key / kTile + 1 : 0;
 }
 
@@ -312,7 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort = reinterpret_cast<volatile int *>(smem + kAbortOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int q0 = blockIdx.x * (kQTiles * kTile);
+  const int q_tiles = p.q_tiles;
+  const int q0 = blockIdx.x * (q_tiles * kTile);
   const int hq = blockIdx.y;
   const int hkv = hq / p.group;
   // key tiles: the prefix's, then the visible ones of the step's own keys
@@ -348,8 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     if (lane == 0) {
       // ---- producer: Q once, then K_j and V_j through two-stage rings ----
-      mbar_expect_tx(bar(kQFull), kQTiles * kTileBytes);
-      for (int t = 0; t < kQTiles; ++t)
+      mbar_expect_tx(bar(kQFull), q_tiles * kTileBytes);
+      for (int t = 0; t < q_tiles; ++t)
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sbase + kQOff + t * kTileBytes + h * kHalfBytes, &tm_q, h * 64, hq, q0 + t * kTile, bar(kQFull));
       const int P = p.page_size;
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(bar(kKFull), 0, abort, p.err);
         if (ok) {
           tc_fence_after();
-          for (int t = 0; t < kQTiles; ++t) {
+          for (int t = 0; t < q_tiles; ++t) {
             qk(t, 0);
             mma_commit(bar(kSFull + t));
           }
@@ -491,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(bar(kVFull + s), (it >> 1) & 1, abort, p.err);
           if (!ok) break;
           const int s1 = (it + 1) & 1;
-          for (int t = 0; t < kQTiles && ok; ++t) {
+          for (int t = 0; t < q_tiles && ok; ++t) {
             ok = mbar_wait(bar(kPReady + t), it & 1, abort, p.err);
             if (!ok) break;
             tc_fence_after();
@@ -519,8 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
-    // ---- softmax warpgroups: warp w handles tile w / 4, tensor-memory lanes 32 (w % 4) .. + 31 ----
+  } else if ((warp >> 2) < q_tiles) {
+    // ---- softmax warpgroups: warp w handles tile w / 4, tensor-memory lanes 32 (w % 4) .. + 31 (the warps of
+    // a tile the CTA does not have go straight to the final barrier) ----
     const int t = warp >> 2;
     const int row = (warp & 3) * 32 + lane;
     const int qi = q0 + t * kTile + row;
@@ -837,6 +842,9 @@ using qe::fail;
 
 namespace qe {
 namespace {
+// Q tiles per CTA (process-wide): 0 = by grid size (default), 1 or 2 forced
+std::atomic<int> g_attention_q_tiles{0};
+
 int paged_attention_impl(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q, int32_t heads_q,
                          const void *k_pool, const void *v_pool, int64_t pool_rows, int32_t heads_kv,
                          const int32_t *block_table, int32_t page_size, int32_t n_prefix, const void *k_local,
@@ -947,7 +955,12 @@ int paged_attention_impl(const void *q, int64_t q_token_stride, int64_t q_head_s
     if (e != cudaSuccess) return cuda_status(e, "qe_paged_attention: smem attribute");
     attr_done[dev].store(true, std::memory_order_relaxed);
   }
-  const dim3 grid(unsigned((n_q + kQTiles * kTile - 1) / (kQTiles * kTile)), unsigned(heads_q));
+  // one-tile CTAs when all of them fit on the SMs at once (twice the CTAs of a grid that would leave most SMs
+  // idle, each CTA with half the work); else two tiles per CTA, whose softmax phases hide each other's
+  int q_tiles = g_attention_q_tiles.load(std::memory_order_relaxed);
+  if (q_tiles == 0) q_tiles = int64_t((n_q + kTile - 1) / kTile) * heads_q <= int64_t(sm_count()) ? 1 : 2;
+  p.q_tiles = q_tiles;
+  const dim3 grid(unsigned((n_q + q_tiles * kTile - 1) / (q_tiles * kTile)), unsigned(heads_q));
   paged_attention_kernel<<<grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
       maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], maps[7], maps[8], p);
   s = cuda_status(cudaGetLastError(), "qe_paged_attention launch");
@@ -967,6 +980,12 @@ extern "C" int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t
                                   block_table, page_size, n_prefix, k_local, v_local, local_token_stride,
                                   local_head_stride, n_local, causal, scale, out, out_token_stride, out_head_stride, lse,
                                   nullptr, err_flag, stream);
+}
+
+extern "C" int qe_set_attention_q_tiles(int32_t q_tiles) {
+  if (q_tiles < 0 || q_tiles > 2) return qe::fail(QE_ERR_INVALID, "qe_set_attention_q_tiles: 0, 1 or 2");
+  qe::g_attention_q_tiles.store(q_tiles, std::memory_order_relaxed);
+  return qe::ok();
 }
 
 extern "C" int qe_paged_attention_append(const void *q, int64_t q_token_stride, int64_t q_head_stride, int32_t n_q,

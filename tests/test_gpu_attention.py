@@ -25,6 +25,16 @@ DEV = "cuda"
 D = 128
 
 
+@pytest.fixture(autouse=True, params=[1, 2], ids=["one_q_tile", "two_q_tiles"])
+def q_tiles(request):
+    """Every test with one and with two 128-query tiles per CTA (by default the grid size picks one)."""
+    from qwenedit_b200 import _lib
+
+    _lib.call("qe_set_attention_q_tiles", request.param)
+    yield request.param
+    _lib.call("qe_set_attention_q_tiles", 0)
+
+
 def _pool(layers, heads, page, n_pages, seed):
     """A page-mode pool of n_pages pages filled with NaN."""
     budget = n_pages * page * layers * 2 * heads * D * 2

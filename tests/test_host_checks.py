@@ -60,8 +60,8 @@ def test_c_abi_rejects_bad_sizes_without_a_gpu():
         _lib.call("qe_latent_crop", None, None, 4, 4, 8, 0, 0, 5, 1, None)
     with pytest.raises(ValueError):
         _lib.call("qe_gather_slots_heads", planes, 1, planes, 1, 48, 32, 16, 16, None, 1, None, None)
-    for fn, bad in (("qe_set_norm_table_mode", 3), ("qe_set_silu_table_mode", 3), ("qe_set_silu_pipeline", 3),
-                    ("qe_set_paged_copy_mode", 5)):
+    for fn, bad in (("qe_set_norm_table_mode", 3), ("qe_set_silu_table_mode", 3), ("qe_set_attention_q_tiles", 3),
+                    ("qe_set_silu_pipeline", 3), ("qe_set_paged_copy_mode", 5)):
         with pytest.raises(ValueError):
             _lib.call(fn, bad)
 
