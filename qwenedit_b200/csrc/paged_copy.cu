@@ -167,14 +167,15 @@ __global__ void __launch_bounds__(kThreads) paged_copy_kernel(CopyParams p) {
   }
 }
 
-// Short rows (eight or more fit in 32 x kRowsUnroll vectors: the 1 KiB encoder rows, 768 B head-sharded DiT rows
-// at 8 GPUs): one warp moves R = (32 kRowsUnroll) / vpr consecutive tokens of one plane per pass, so each
-// lane still has kRowsUnroll loads in flight. Lane i < R holds token i's slot; the other lanes read it with a
+// Short rows (eight or more fit in 32 x kUnroll vectors: the 1 KiB encoder rows, 768 B head-sharded DiT rows
+// at 8 GPUs): one warp moves R = (32 kUnroll) / vpr consecutive tokens of one plane per pass, so each
+// lane still has kUnroll loads in flight (16 of 16 bytes, or 8 of 32 bytes on 32-byte aligned planes: the same
+// bytes with half the memory instructions). Lane i < R holds token i's slot; the other lanes read it with a
 // shuffle. On the contiguous side (the gather output, the append source) the R rows are one run, so those
 // accesses stay fully coalesced across row boundaries.
 constexpr int kRowsUnroll = 16;
 
-template <typename V, int kMode, bool kGather, bool kPtrs>
+template <typename V, int kMode, bool kGather, bool kPtrs, int kUnroll = kRowsUnroll>
 __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p, int32_t rows_per_pass) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
@@ -207,13 +208,13 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
     if (other_plane == nullptr) continue;  // pointer form: null or misaligned source plane, skipped and reported
     // the R rows of the pass are one run on the contiguous side: vector v of the pass is run[v]
     V *run = reinterpret_cast<V *>(const_cast<char *>(other_plane) + t0 * p.row_bytes);
-    V buf[kRowsUnroll];
+    V buf[kUnroll];
     uint32_t valid = 0u;
     // (row, vector) of vector lane + 32 k of the pass, advanced by 32 per k
     int ri = int(lane / vpr);
     int64_t vec = lane - int64_t(ri) * vpr;
 #pragma unroll
-    for (int k = 0; k < kRowsUnroll; ++k) {
+    for (int k = 0; k < kUnroll; ++k) {
       const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
       if (ri < R && slot >= 0) {
         valid |= 1u << k;
@@ -228,13 +229,13 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
     }
     if (kGather) {
 #pragma unroll
-      for (int k = 0; k < kRowsUnroll; ++k)
+      for (int k = 0; k < kUnroll; ++k)
         if (valid & (1u << k)) store_v<V>(run + lane + 32 * k, buf[k]);
     } else {  // walk the pass again for the pool rows
       ri = int(lane / vpr);
       vec = lane - int64_t(ri) * vpr;
 #pragma unroll
-      for (int k = 0; k < kRowsUnroll; ++k) {
+      for (int k = 0; k < kUnroll; ++k) {
         const int64_t slot = __shfl_sync(0xffffffffu, my_slot, ri < 32 ? ri : 0);
         if (valid & (1u << k)) store_v<V>(reinterpret_cast<V *>(pool_plane + slot * p.row_bytes) + vec, buf[k]);
         vec += 32;
@@ -603,12 +604,13 @@ int launch_unrolled(const CopyParams &p, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "paged copy launch");
 }
 
-template <typename V, int kMode, bool kGather, bool kPtrs>
+template <typename V, int kMode, bool kGather, bool kPtrs, int kUnroll = kRowsUnroll>
 int launch_rows(const CopyParams &p, int rows_per_pass, cudaStream_t stream) {
   static std::atomic<int> cached_blocks{0};
   int blocks_per_sm = cached_blocks.load(std::memory_order_relaxed);
   if (blocks_per_sm == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, paged_copy_rows_kernel<V, kMode, kGather, kPtrs>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm,
+                                                      paged_copy_rows_kernel<V, kMode, kGather, kPtrs, kUnroll>,
                                                       kThreads, 0) != cudaSuccess ||
         blocks_per_sm <= 0)
       blocks_per_sm = 2;
@@ -618,7 +620,7 @@ int launch_rows(const CopyParams &p, int rows_per_pass, cudaStream_t stream) {
   const int64_t warps_per_block = kThreads / 32;
   int64_t blocks = std::min<int64_t>((items + warps_per_block - 1) / warps_per_block, int64_t(sm_count()) * blocks_per_sm);
   blocks = std::max<int64_t>(blocks, 1);
-  paged_copy_rows_kernel<V, kMode, kGather, kPtrs>
+  paged_copy_rows_kernel<V, kMode, kGather, kPtrs, kUnroll>
       <<<dim3(unsigned(blocks)), dim3(kThreads), 0, stream>>>(p, int32_t(rows_per_pass));
   return cuda_status(cudaGetLastError(), "paged copy launch");
 }
@@ -648,6 +650,11 @@ int launch(const CopyParams &p, int align, cudaStream_t stream) {
   // (the same bytes as 16 of 16 bytes, half the instructions and L1 requests)
   if (align >= 32 && mode != 4 && (p.row_bytes > 1024 || mode == 3))
     return launch_unrolled<Vec32, kMode, kGather, kPtrs, 8>(p, stream);
+  // rows of at most 1 KiB on 32-byte aligned planes (eight or more per warp pass): the short-row kernel with
+  // 256-bit vectors, 8 per lane in flight
+  if (align >= 32 && mode != 4 && 32 * 8 / (p.row_bytes / 32) >= 8)
+    return launch_rows<Vec32, kMode, kGather, kPtrs, 8>(
+        p, int(std::min<int64_t>(32 * 8 / (p.row_bytes / 32), 32)), stream);
   if (align >= 16) return launch_typed<int4, kMode, kGather, kPtrs>(p, stream);
   if (align >= 4) return launch_typed<uint32_t, kMode, kGather, kPtrs>(p, stream);
   return launch_typed<uint8_t, kMode, kGather, kPtrs>(p, stream);
