@@ -128,8 +128,8 @@ int qe_gather_slots_heads(qe_planes pool, int64_t pool_rows, qe_planes out, int3
                           int64_t n_tokens, int32_t *err_flag, void *stream);
 
 /* Kernel used by the copies above (process-wide): 0 = default, 1 = warp-vectorised LDG/STG kernel (rows of at
- * most 1 KiB are moved several per warp pass; rows above 1 KiB on 32-byte aligned planes move in 256-bit
- * vectors, else 16-byte ones), 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned
+ * most 1 KiB are moved several per warp pass; on 32-byte aligned planes in 256-bit vectors, else 16-byte
+ * ones), 2 = TMA bulk-copy pipeline (cp.async.bulk through shared memory; 16-byte aligned
  * rows of <= 32 KiB, else the warp kernel), 3 = the warp kernel with one row per warp pass whatever the row
  * size, 4 = the warp kernel with 16-byte vectors only (also for qe_gather_slots_heads). No counterpart in the
  * reference; for measurement and tuning. */
