@@ -243,8 +243,9 @@ int qe_paged_attention(const void *q, int64_t q_token_stride, int64_t q_head_str
  * qe_paged_attention plus append_table, device int32 page ids, ceil(n_local / page_size) of them; own token t
  * (row t of k_local / v_local) is written to pool row append_table[t / page_size] * page_size + t % page_size of
  * k_pool and v_pool (page_size and the pool planes as above; block_table may be null when n_prefix == 0).
- * Rows of the last page past own token n_local - 1 are not written. One CTA per K/V head stores the K and V tiles
- * it has loaded for the attention, so the own K/V are read from HBM once for both. Pages outside the pool are
+ * Rows of the last page past own token n_local - 1 are not written. Each own K/V tile is stored by exactly one
+ * of the CTAs that load it for the attention (spread over the query-tile CTAs and the query heads of its group),
+ * from the same shared-memory stage, so the own K/V are read from HBM once for both. Pages outside the pool are
  * skipped and set bit 1 of *err_flag (err_flag must not be null). Needs n_q >= 1 and n_local >= 1. Replaces the
  * separate store of freshly computed prefix K/V after the forward (multi_turn/cache/prefill.py:69-72, the
  * encoder's _store, multi_turn/cache/encoder.py:131-138); no counterpart as one operation in the reference. */
