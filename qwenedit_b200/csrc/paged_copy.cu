@@ -7,10 +7,10 @@
 //
 // A pool is a stack of planes (layer x {K,V}), each [rows, row_bytes]; a token's K or V for one layer is
 // one row of H*D elements (6 KB for the Qwen-Image DiT, 1 KB for the text encoder). Every row copy is
-// a vectorised, fully coalesced warp copy, all loads of a pass issued before the matching stores: rows above
-// 1 KiB on 32-byte aligned planes move in 256-bit vectors (lane i: bytes [32 i, 32 i + 32) of each 1 KiB
-// stripe, 8 in flight per lane), other rows in 16-byte vectors (lane i: bytes [16 i, 16 i + 16) of each
-// 512-byte stripe, 8 or 16 in flight per lane; rows of at most 1 KiB several per warp pass). Each warp walks its
+// a vectorised, fully coalesced warp copy, all loads of a pass issued before the matching stores: on 32-byte
+// aligned planes rows move in 256-bit vectors (lane i: bytes [32 i, 32 i + 32) of each 1 KiB stripe, 8 in
+// flight per lane), else in 16-byte vectors (lane i: bytes [16 i, 16 i + 16) of each 512-byte stripe, 8 or 16
+// in flight per lane); rows of at most 1 KiB go several per warp pass. Each warp walks its
 // rows through the slot list (token-granular, page_size 1) or the block table (page_size P). The grid is
 // persistent: a multiple of the SM count, warps striding over the (plane, token) rows.
 #include <algorithm>
@@ -252,8 +252,9 @@ __global__ void __launch_bounds__(kThreads) paged_copy_rows_kernel(CopyParams p,
 // = pool row slots[t] of plane, head h. For the text encoder's partial hit (cache/encoder.py:173-182), which
 // gathers the prefix [L, 2, m, H, D] and then, per layer, transposes it and concatenates the tail K/V into a
 // fresh [1, H, m + n, D] tensor: written here once, straight into a [L, 2, H, m + n, D] buffer whose last n
-// positions the caller fills per layer. One warp moves R consecutive tokens of one plane per pass (16-byte
-// vectors, 16 per lane in flight); lane i < R holds token i's slot.
+// positions the caller fills per layer. One warp moves R consecutive tokens of one plane per pass (256-bit
+// vectors, 8 per lane in flight, when every address is 32-byte aligned; else 16-byte vectors, 16 in flight);
+// lane i < R holds token i's slot.
 struct HeadsParams {
   Planes pool;
   Planes out;

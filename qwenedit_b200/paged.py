@@ -152,8 +152,8 @@ COPY_MODES = {"auto": 0, "warp": 1, "bulk": 2, "warp_row": 3, "warp16": 4}
 
 def set_copy_mode(mode: str) -> None:
     """Select the paged copy kernel process-wide: "auto", "warp" (vectorised LDG/STG, short rows several per warp
-    pass, 256-bit vectors for rows above 1 KiB on 32-byte aligned planes), "bulk" (TMA bulk copies), "warp_row"
-    (the warp kernel, one row per warp pass) or "warp16" (the warp kernel with 16-byte vectors only)."""
+    pass, 256-bit vectors on 32-byte aligned planes), "bulk" (TMA bulk copies), "warp_row" (the warp kernel, one
+    row per warp pass) or "warp16" (the warp kernel and the head-major gather with 16-byte vectors only)."""
     _lib.call("qe_set_paged_copy_mode", COPY_MODES[mode])
 
 
